@@ -1,0 +1,354 @@
+#!/usr/bin/env python
+"""Benchmark of the MoE layer hot path: routing -> permute -> expert FFN -> combine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config prefill] [--impl ours|reference]
+
+Metric: MoE layer tokens/s on the headline configuration T=4096, H=2048, E=16,
+K=2, I=8192 (fp16 in/out, fp32 accumulation), synthetic seeded inputs with the
+benchmark's distributions.  A step is one full layer forward over one batch.
+
+* ``value``: whole-job tokens/s with inputs resident in HBM, device time of the K
+  timed steps (CUDA events, max over ranks), L2 flushed between steps.
+* ``e2e``: the same through the public API with the step's x copied host->device
+  from pinned memory and y copied back inside the timed region.
+* ``roofline``: the dominant kernel (gate/up grouped GEMM + SwiGLU), its FLOP/s
+  from the stage events of the timed steps against the measured bf16/fp16 peak.
+* ``cpu_baseline``: the reference's own CPU code (tests/moe_cpu_sim.cpp NaiveMoE,
+  compiled into oracle/_ref) on a bounded token slice, rank 0 at N=1 only.
+
+``--impl reference`` times that CPU reference alone (all host threads) and prints
+the same JSON line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+METRIC = "MoE layer tokens/s (T=4096,H=2048,E=16,K=2,I=8192); FFN % FP16 TC peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.isfile(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(key):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/)."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if not os.path.isfile(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == key:
+                try:
+                    return float(parts[1])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.tmp is None:
+            return None
+        self.tmp.flush()
+        with open(self.tmp.name) as f:
+            rows = [r.split(",") for r in f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = max(smax, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        load = [v for v in sm if v > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ============================================================================ reference arm
+def reference_inputs(cfg, moe):
+    """The configuration's inputs as fp32 numpy (fp16-rounded values), drawn on the CPU."""
+    import numpy as np
+
+    T, H, E, K, I, seed = moe.CONFIGS[cfg]
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device="cpu")
+    return (x.float().numpy(), wg.float().numpy(), ew.float().numpy().astype(np.float32, copy=False)), \
+        (T, H, E, K, I)
+
+
+def cpu_reference_timer(cfg, moe):
+    """(timer object, kind): the reference's NaiveMoE (oracle/_ref) or, when that was
+    not built, the C restatement (oracle/_build)."""
+    from oracle import oracle as O
+
+    (x, wg, ew), (T, H, E, K, I) = reference_inputs(cfg, moe)
+    if O.ref_available():
+        t = O.RefTimer(x, wg, ew, K)
+        return (lambda t0, t1, th: t.naive(t0, t1, th)), "reference", (T, H, E, K, I), t
+    def run(t0, t1, th):
+        return O.moe_naive(x[t0:t1], wg, ew, K, nthreads=th)[0]
+    return run, "port", (T, H, E, K, I), None
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    moe = __import__("_moe_loader").load()
+    run, kind, (T, H, E, K, I), keep = cpu_reference_timer(args.config, moe)
+    threads = os.cpu_count() or 1
+    sample = args.ref_tokens
+    times = []
+    t0 = 0
+    for step in range(args.warmup + args.steps):
+        a = t0 % T
+        b = min(a + sample, T)
+        s = time.perf_counter()
+        run(a, b, threads)
+        dt = time.perf_counter() - s
+        if step >= args.warmup:
+            times.append((b - a) / dt)
+        t0 += sample
+    value = statistics.mean(times)
+    ms_per_step = 1000.0 * sample / value
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I}; each step = NaiveMoE on a "
+                               f"{sample}-token slice", "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{sample} tokens of the {args.config} batch per step, NaiveMoE "
+                                   f"(tests/moe_cpu_sim.cpp:183-306) split over {threads} threads"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    if keep is not None:
+        keep.close()
+    return 0
+
+
+# ============================================================================ our arm
+def cpu_baseline_sample(args, moe):
+    """The reference's CPU code on a bounded slice of the same workload (rank 0, N=1)."""
+    run, kind, (T, H, E, K, I), keep = cpu_reference_timer(args.config, moe)
+    threads = os.cpu_count() or 1
+    sample = args.ref_tokens
+    run(0, min(threads, T), threads)  # warm-up: page in the weights
+    s = time.perf_counter()
+    run(0, sample, threads)
+    dt = time.perf_counter() - s
+    if keep is not None:
+        keep.close()
+    return {"value": sample / dt, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"first {sample} tokens of the {args.config} batch, NaiveMoE "
+                      f"(tests/moe_cpu_sim.cpp:183-306) over {threads} threads, {dt:.2f} s"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    moe = __import__("_moe_loader").load()
+    T, H, E, K, I, seed = moe.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    # every rank runs the layer on its own batch (per-GPU work fixed as N grows)
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed + rank, device=dev)
+    ws = torch.empty((moe.moe_layer_workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
+    y = torch.empty((T, H), dtype=torch.float16, device=dev)
+    flush = torch.empty((L2_FLUSH_BYTES,), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        moe.moe_layer_forward(x, wg, ew, K, y=y, workspace=ws)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if moe.device_error(ws) != 0:
+        raise RuntimeError("device error during warm-up")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        moe.trace_start(args.steps)
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        stages = moe.trace_stop(args.steps)
+        if world > 1:
+            dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if moe.device_error(ws) != 0:
+        raise RuntimeError("device error during the timed steps")
+
+    # end to end: pinned host x in, y back to pinned host, every step
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, H), dtype=torch.float16).pin_memory()
+    x_in = torch.empty_like(x)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        j = i - args.warmup
+        if j >= 0:
+            e_starts[j].record(stream)
+        x_in.copy_(x_host, non_blocking=True)
+        moe.moe_layer_forward(x_in, wg, ew, K, y=y, workspace=ws)
+        y_host.copy_(y, non_blocking=True)
+        if j >= 0:
+            e_ends[j].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
+
+    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        ms = total_ms / args.steps
+        value = world * T * args.steps / (total_ms / 1e3)
+        e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+        stage_avg = {k: statistics.mean(c[k] for c in stages) for k in moe.TRACE_STAGES}
+        g1_flops = 2.0 * T * K * H * 2 * I
+        g2_flops = 2.0 * T * K * I * H
+        g1_ms = stage_avg["gemm_swiglu"]
+        ach = g1_flops / (g1_ms / 1e3) / 1e12
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        ffn_ms = stage_avg["gemm_swiglu"] + stage_avg["gemm_down"]
+        ffn_tf = (g1_flops + g2_flops) / (ffn_ms / 1e3) / 1e12
+        traffic = load_traffic(f"gemm_swiglu_{args.config}")
+        hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        comb_bytes = T * K * H * 2 + T * K * 2 + T * H * 2
+        rout_bytes = T * H * 2 + H * E * 2 + T * K * 6
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I} per GPU",
+                       "global_batch": world * T, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "flushed between timed steps (512 MB write)", "inputs": "seeded N(0,1)/N(0,1/fan_in) fp16"},
+            "roofline": {"kernel": "gemm_swiglu (gate/up grouped GEMM + SwiGLU epilogue)", "bound": "tensor",
+                         "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                         "peak_source": f"{peak_src} bf16_tflops (burst cuBLAS)",
+                         "traffic": traffic},
+            "ffn": {"tflops": ffn_tf, "frac_of_peak": ffn_tf / peak, "ms": ffn_ms,
+                    "frac_of_datasheet_2250": ffn_tf / 2250.0},
+            "stages_ms": stage_avg,
+            "hbm_kernels": {"combine_gbs": comb_bytes / (stage_avg["combine"] / 1e3) / 1e9 if stage_avg["combine"] else None,
+                            "routing_gbs": rout_bytes / (stage_avg["routing"] / 1e3) / 1e9 if stage_avg["routing"] else None,
+                            "hbm_peak_gbs": hbm},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": args.steps * 8,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline_sample(args, moe)
+            except Exception as exc:  # reported, never fatal for the GPU number
+                line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="prefill")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-tokens", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

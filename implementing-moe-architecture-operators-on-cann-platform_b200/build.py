@@ -1,0 +1,58 @@
+"""Builds the sm_100a shared library libmoe_b200.so in-tree with nvcc.
+
+Every kernel is compiled for sm_100a only (tcgen05 / TMA code has no other
+target).  The library exports the C ABI declared in include/moe_ops.h.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libmoe_b200.so")
+
+SOURCES = ["routing.cu", "permute.cu", "grouped_gemm.cu", "combine.cu", "moe_ops.cu"]
+HEADERS = ["moe_common.cuh", "moe_kernels.h"]
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+         "--expt-relaxed-constexpr", "-Xptxas", "-v"] if os.environ.get("MOE_PTXAS_VERBOSE") else \
+        ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
+
+
+def _stale(out: str, deps: list[str]) -> bool:
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    include = os.path.join(os.path.dirname(HERE), "include")
+    hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(include, "moe_ops.h")]
+    objs = []
+    for src in SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src.replace(".cu", ".o"))
+        objs.append(o)
+        if _stale(o, [s] + hdrs):
+            cmd = [NVCC, *ARCH, *FLAGS, "-I", include, "-c", s, "-o", o]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.check_call(cmd)
+    if _stale(LIB, objs):
+        cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.check_call(cmd)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose=True))
+    sys.exit(0)

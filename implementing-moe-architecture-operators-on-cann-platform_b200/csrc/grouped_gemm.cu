@@ -1,0 +1,452 @@
+// grouped_gemm.cu -- the expert FFN as two grouped GEMMs on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
+//
+// Replaces op_kernel/moe_expert_ffn.cpp (Ascend MatmulImpl with a GM workspace
+// between a gate/up stage and a down stage, :265-394).  Math, per expert e and
+// per permuted row r of that expert (tests/moe_cpu_sim.cpp:262-294):
+//   GEMM1 (MODE_SWIGLU): h[r, i]  = silu(xp[r,:] . Wg_e[i,:]) * (xp[r,:] . Wu_e[i,:])
+//   GEMM2 (MODE_DOWN)  : out[perm[r], n] = h[r,:] . Wd_e[n,:]
+// with Wg_e, Wu_e = [I,H] and Wd_e = [H,I] row-major slices of expert_weights
+// [E, 3I, H] (the reference CPU oracle's layout).  Every operand is K-major, so
+// no weight is transposed or repacked: TMA reads them in place.
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0      : TMA producer -- per k-block, one 128x64 box of A and two
+//                 128x64 boxes of B (gate rows + up rows for GEMM1, two halves of
+//                 256 down rows for GEMM2) into a STAGES-deep shared-memory ring;
+//   warp 1      : TMEM allocator + single-thread UMMA issuer, M=128 N=256 K=16
+//                 instructions accumulating in fp32 in TMEM; two accumulator
+//                 buffers of 256 columns so the epilogue of tile i overlaps the
+//                 main loop of tile i+1;
+//   warps 2..5  : epilogue -- tcgen05.ld of the warp's 32 TMEM lanes (= rows),
+//                 SwiGLU in fp32 (GEMM1) or plain conversion (GEMM2), fp16 stores;
+//                 GEMM2 scatters each row to expert_out[t, k, :] through perm.
+// Tiles are (expert, n-tile, m-tile) with m innermost, so the CTAs working at the
+// same time share one weight tile in L2 and every weight byte comes from HBM once.
+// The tile list is derived on the device from offsets[] (no host sync).
+//
+// No TMA multicast and no cluster launch are used: the same kernel runs on every
+// rank of the expert-parallel path.
+#include "moe_common.cuh"
+#include "moe_kernels.h"
+
+namespace moe {
+
+constexpr int GM_BM = 128;        // rows per tile (UMMA M)
+constexpr int GM_BN = 256;        // accumulator columns per tile (UMMA N)
+constexpr int GM_BK = 64;         // k per stage: 64 fp16 = one 128-byte swizzle row
+constexpr int GM_STAGES = 4;
+constexpr int GM_A_BYTES = GM_BM * GM_BK * 2;          // 16 KB
+constexpr int GM_BHALF_BYTES = 128 * GM_BK * 2;        // 16 KB
+constexpr int GM_STAGE_BYTES = GM_A_BYTES + 2 * GM_BHALF_BYTES;  // 48 KB
+constexpr int GM_TMEM_COLS = 512;  // two 256-column fp32 accumulators
+constexpr int GM_THREADS = 192;
+constexpr int GM_MAX_E = 256;
+
+struct GemmArgs {
+    const int32_t* offsets;  // [E+1] permuted-row boundaries per expert
+    const int32_t* perm;     // [rows] flat source index t*K+k per permuted row
+    __half* out;             // GEMM1: h [rows, I]; GEMM2: expert_out [T*K, H]
+    int* err;
+    int E;
+    int kdim;                // H for GEMM1, I for GEMM2
+    int nvalid;              // I for GEMM1, H for GEMM2 (valid output columns)
+    int n_tiles;             // N tiles per expert
+    int b_rows_per_expert;   // 3I (GEMM1, B view [E*3I, H]) or 3H (GEMM2, B view [E*3H, I])
+    int b_seg;               // first B row of the segment inside an expert: 0 or 2H
+    int b_nstep;             // B rows advanced per N tile: 128 (GEMM1) or 256 (GEMM2)
+    int b_hi_delta;          // row distance of the second B box: I (up rows) or 128
+    int out_ld;              // leading dimension of out: I or H
+};
+
+struct GemmSmemTail {
+    uint64_t full[GM_STAGES];
+    uint64_t empty[GM_STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+    int tile_prefix[GM_MAX_E + 1];
+};
+
+__host__ __device__ constexpr size_t gemm_smem_bytes()
+{
+    return 1024 + (size_t)GM_STAGES * GM_STAGE_BYTES + sizeof(GemmSmemTail);
+}
+
+// Maps a CTA-visited tile index to (expert, m tile, n tile).  Tile indices a
+// CTA visits only grow, so the expert cursor only moves forward.
+struct TileCursor {
+    int e = 0;
+    __device__ __forceinline__ void decode(const int* prefix, const int32_t* offsets, int n_tiles,
+                                           int tile, int& e_out, int& mt, int& nt)
+    {
+        while (tile >= prefix[e + 1]) e++;
+        const int cnt = offsets[e + 1] - offsets[e];
+        const int mts = (cnt + GM_BM - 1) / GM_BM;
+        const int local = tile - prefix[e];
+        nt = local / mts;
+        mt = local - nt * mts;
+        e_out = e;
+    }
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmArgs args)
+{
+    extern __shared__ uint8_t gm_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(gm_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + GM_STAGES * GM_STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int E = args.E;
+    const int32_t* __restrict__ offsets = args.offsets;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GM_STAGES; s++) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->empty[s]), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(smem_u32(&tail->tfull[a]), 1);
+            mbar_init(smem_u32(&tail->tempty[a]), 128);
+        }
+        mbar_init(smem_u32(&tail->drain), 1);
+        tail->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 2) {  // tile prefix: tiles per expert = ceil(rows/128) * n_tiles
+        if (lane == 0) {
+            int run = 0;
+            for (int e = 0; e < E; e++) {
+                tail->tile_prefix[e] = run;
+                const int cnt = offsets[e + 1] - offsets[e];
+                run += ((cnt + GM_BM - 1) / GM_BM) * args.n_tiles;
+            }
+            tail->tile_prefix[E] = run;
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tail->tmem_base), GM_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t tmem_base = tail->tmem_base;
+    const int total_tiles = tail->tile_prefix[E];
+    const int nk = (args.kdim + GM_BK - 1) / GM_BK;
+    volatile int* abort_flag = &tail->abort_flag;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t pol_a = l2_policy_evict_last();  // activations: reused by every N tile
+            const uint64_t pol_b = l2_policy_evict_first(); // weights: read by the m tiles in flight
+            TileCursor cur;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+                int e, mt, nt;
+                cur.decode(tail->tile_prefix, offsets, args.n_tiles, tile, e, mt, nt);
+                const int a_row = offsets[e] + mt * GM_BM;
+                const int b_lo = e * args.b_rows_per_expert + args.b_seg + nt * args.b_nstep;
+                const int b_hi = b_lo + args.b_hi_delta;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % GM_STAGES;
+                    const uint32_t par = ((it / GM_STAGES) & 1u) ^ 1u;
+                    if (!mbar_wait_bounded(smem_u32(&tail->empty[s]), par, args.err,
+                                           MOE_DEV_WAIT_TIMEOUT_TMA, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = smem_u32(&tail->full[s]);
+                    uint8_t* st = smem + s * GM_STAGE_BYTES;
+                    mbar_arrive_expect_tx(full, GM_STAGE_BYTES);
+                    tma_load_2d(smem_u32(st), &tmA, full, kb * GM_BK, a_row, pol_a);
+                    tma_load_2d(smem_u32(st + GM_A_BYTES), &tmB, full, kb * GM_BK, b_lo, pol_b);
+                    tma_load_2d(smem_u32(st + GM_A_BYTES + GM_BHALF_BYTES), &tmB, full, kb * GM_BK,
+                                b_hi, pol_b);
+                }
+            }
+            if (!ok) {
+                // Unwinding after a timeout: wait (bounded) until the copies this
+                // thread issued into the ring have landed before the CTA exits.
+                const uint32_t first = it > GM_STAGES ? it - GM_STAGES : 0;
+                for (uint32_t j = first; j < it; j++) {
+                    const uint64_t t0 = global_timer_ns();
+                    while (!mbar_try_wait(smem_u32(&tail->full[j % GM_STAGES]), (j / GM_STAGES) & 1u))
+                        if (global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16_f32(GM_BM, GM_BN);
+            uint32_t it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, lt++) {
+                const uint32_t acc = lt & 1u;
+                if (!mbar_wait_bounded(smem_u32(&tail->tempty[acc]), ((lt >> 1) & 1u) ^ 1u, args.err,
+                                       MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * GM_BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % GM_STAGES;
+                    if (!mbar_wait_bounded(smem_u32(&tail->full[s]), (it / GM_STAGES) & 1u, args.err,
+                                           MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * GM_STAGE_BYTES);
+                    const uint32_t b_addr = a_addr + GM_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < GM_BK / 16; k++) {
+                        // advancing K by 16 fp16 = 32 bytes inside the 128-byte swizzle row
+                        umma_f16_ss(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                    idesc, (kb | k) != 0);
+                    }
+                    umma_commit(smem_u32(&tail->empty[s]));  // frees the stage when these MMAs finish
+                }
+                if (ok) umma_commit(smem_u32(&tail->tfull[acc]));  // accumulator ready
+            }
+            // Make sure no MMA of this CTA is still running before TMEM is freed.
+            umma_commit(smem_u32(&tail->drain));
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(smem_u32(&tail->drain), 0))
+                if (global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) {
+                    atomicOr(args.err, MOE_DEV_WAIT_TIMEOUT_MMA);
+                    break;
+                }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3;            // TMEM lane quarter this warp may access
+        const int r = q * 32 + lane;       // row inside the tile
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        TileCursor cur;
+        uint32_t lt = 0;
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
+            int e, mt, nt;
+            cur.decode(tail->tile_prefix, offsets, args.n_tiles, tile, e, mt, nt);
+            const uint32_t acc = lt & 1u;
+            if (!mbar_wait_bounded(smem_u32(&tail->tfull[acc]), (lt >> 1) & 1u, args.err,
+                                   MOE_DEV_WAIT_TIMEOUT_EPI, abort_flag))
+                break;
+            tc_fence_after();
+            const int row0 = offsets[e] + mt * GM_BM;
+            const int rows = min(GM_BM, offsets[e + 1] - row0);
+            const bool valid = r < rows;
+            const uint32_t tbase = tmem_base + acc * GM_BN + lane_off;
+            if (MODE == MODE_SWIGLU) {
+                const int col0 = nt * 128;
+                __half* dst = args.out + (size_t)(row0 + r) * args.out_ld + col0;
+#pragma unroll 1
+                for (int j = 0; j < 4; j++) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_32x32b_x32(tbase + j * 32, g);
+                    tmem_ld_32x32b_x32(tbase + 128 + j * 32, u);
+                    tmem_ld_wait();
+                    if (valid) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int c = 0; c < 16; c++) {
+                            const float g0 = __uint_as_float(g[2 * c]), g1 = __uint_as_float(g[2 * c + 1]);
+                            const float u0 = __uint_as_float(u[2 * c]), u1 = __uint_as_float(u[2 * c + 1]);
+                            // silu(g) = g / (1 + exp(-g)), tests/moe_cpu_sim.cpp:155-158
+                            const float h0 = g0 / (1.0f + expf(-g0)) * u0;
+                            const float h1 = g1 / (1.0f + expf(-g1)) * u1;
+                            pk[c] = pack_half2(h0, h1);
+                        }
+                        const int cb = col0 + j * 32;
+#pragma unroll
+                        for (int v = 0; v < 4; v++)
+                            if (cb + v * 8 + 8 <= args.nvalid)
+                                *reinterpret_cast<uint4*>(dst + j * 32 + v * 8) =
+                                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                    }
+                }
+            } else {
+                const int col0 = nt * GM_BN;
+                __half* dst = nullptr;
+                if (valid) dst = args.out + (size_t)args.perm[row0 + r] * args.out_ld + col0;
+#pragma unroll 1
+                for (int j = 0; j < 8; j++) {
+                    uint32_t v32[32];
+                    tmem_ld_32x32b_x32(tbase + j * 32, v32);
+                    tmem_ld_wait();
+                    if (valid) {
+                        const int cb = col0 + j * 32;
+#pragma unroll
+                        for (int v = 0; v < 4; v++) {
+                            if (cb + v * 8 + 8 <= args.nvalid) {
+                                uint4 o;
+                                o.x = pack_half2(__uint_as_float(v32[8 * v + 0]), __uint_as_float(v32[8 * v + 1]));
+                                o.y = pack_half2(__uint_as_float(v32[8 * v + 2]), __uint_as_float(v32[8 * v + 3]));
+                                o.z = pack_half2(__uint_as_float(v32[8 * v + 4]), __uint_as_float(v32[8 * v + 5]));
+                                o.w = pack_half2(__uint_as_float(v32[8 * v + 6]), __uint_as_float(v32[8 * v + 7]));
+                                *reinterpret_cast<uint4*>(dst + j * 32 + v * 8) = o;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tail->tempty[acc]));
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, GM_TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 tensor [rows, inner] (inner contiguous), 64 x 128 boxes, 128-byte swizzle,
+// zero fill outside the tensor.
+static bool make_tmap(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t rows)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {GM_BK, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static int sm_count()
+{
+    static int n[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (n[dev] <= 0) n[dev] = 148;
+    }
+    return n[dev];
+}
+
+template <int MODE>
+static cudaError_t set_gemm_attr()
+{
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_kernel<MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gemm_smem_bytes());
+    if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+    return e;
+}
+
+int grid_for(int rows_cap, int E, int n_tiles, int max_ctas)
+{
+    long long upper = (long long)n_tiles * ((rows_cap + GM_BM - 1) / GM_BM + E);
+    int sms = sm_count();
+    if (max_ctas > 0 && max_ctas < sms) sms = max_ctas;
+    return (int)(upper < sms ? (upper > 0 ? upper : 1) : sms);
+}
+
+// GEMM1: h[rows, I] = SwiGLU(xp @ [Wg; Wu]^T) per expert.
+cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, const int32_t* offsets,
+                               __half* h, int* err, int rows_cap, int H, int E, int I, int max_ctas,
+                               cudaStream_t s)
+{
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, xp, (uint64_t)H, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
+        !make_tmap(&tb, expert_weights, (uint64_t)H, (uint64_t)E * 3 * I))
+        return cudaErrorInvalidValue;
+    cudaError_t e = set_gemm_attr<MODE_SWIGLU>();
+    if (e != cudaSuccess) return e;
+    GemmArgs a;
+    a.offsets = offsets;
+    a.perm = nullptr;
+    a.out = h;
+    a.err = err;
+    a.E = E;
+    a.kdim = H;
+    a.nvalid = I;
+    a.n_tiles = (I + 127) / 128;
+    a.b_rows_per_expert = 3 * I;
+    a.b_seg = 0;
+    a.b_nstep = 128;
+    a.b_hi_delta = I;
+    a.out_ld = I;
+    const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
+    ffn_gemm_kernel<MODE_SWIGLU><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+// GEMM2: expert_out[perm[r], :] = h[r, :] @ Wd^T per expert.
+cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
+                             const int32_t* perm, __half* expert_out, int* err, int rows_cap, int H,
+                             int E, int I, int max_ctas, cudaStream_t s)
+{
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
+        !make_tmap(&tb, expert_weights, (uint64_t)I, (uint64_t)E * 3 * H))
+        return cudaErrorInvalidValue;
+    cudaError_t e = set_gemm_attr<MODE_DOWN>();
+    if (e != cudaSuccess) return e;
+    GemmArgs a;
+    a.offsets = offsets;
+    a.perm = perm;
+    a.out = expert_out;
+    a.err = err;
+    a.E = E;
+    a.kdim = I;
+    a.nvalid = H;
+    a.n_tiles = (H + GM_BN - 1) / GM_BN;
+    a.b_rows_per_expert = 3 * H;
+    a.b_seg = 2 * H;
+    a.b_nstep = GM_BN;
+    a.b_hi_delta = 128;
+    a.out_ld = H;
+    const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
+    ffn_gemm_kernel<MODE_DOWN><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,34 @@
+// moe_kernels.h -- internal launch wrappers shared by the kernel files and the
+// C-ABI host layer (moe_ops.cu).  Not part of the public interface.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+enum GemmMode { MODE_SWIGLU = 0, MODE_DOWN = 1 };
+
+cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights,
+                           int T, int H, int E, int K, cudaStream_t s);
+
+cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
+                           int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,
+                           int* err, cudaStream_t s);
+
+cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* offsets, int E,
+                               int K, int H, int rows_cap, __half* xp, cudaStream_t s);
+
+cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights,
+                               const int32_t* offsets, __half* h, int* err, int rows_cap, int H,
+                               int E, int I, int max_ctas, cudaStream_t s);
+
+cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
+                             const int32_t* perm, __half* expert_out, int* err, int rows_cap,
+                             int H, int E, int I, int max_ctas, cudaStream_t s);
+
+cudaError_t launch_combine(const __half* expert_out, const __half* weights, __half* y, int T,
+                           int H, int K, cudaStream_t s);
+
+}  // namespace moe

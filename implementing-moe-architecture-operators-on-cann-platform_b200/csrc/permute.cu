@@ -1,0 +1,153 @@
+// permute.cu -- bit-exact stable counting sort of (token, slot) pairs by expert id,
+// and the row gather that lays the tokens of each expert out contiguously.
+//
+// Reference behaviour: the Ascend FFN kernel scans expert_ids once per expert
+// (op_kernel/moe_expert_ffn.cpp:186-195) and the CPU simulation builds the same
+// list (tests/moe_cpu_sim.cpp:412-419): experts ascending, and inside one expert
+// the flat index t*K+k ascending.  A stable counting sort over the flat index
+// produces exactly that order in O(T*K) instead of O(E*T*K), with no
+// 512-per-expert cap (the reference's MAX_TOKENS_PER_EXPERT truncation).
+//
+// Three passes over the ids (a few microseconds even at T*K = 98304):
+//   1. count   : per chunk of PC flat entries, a histogram over experts
+//   2. scan    : per expert, exclusive prefix over chunks -> chunk bases and the
+//                expert boundaries offsets[E+1]
+//   3. scatter : within a chunk, the stable rank of each entry among the entries
+//                with the same expert (warp match + per-warp prefix)
+// then a gather copies x[perm[r]/K, :] to row r of the permuted activations.
+#include "moe_common.cuh"
+#include "moe_kernels.h"
+
+namespace moe {
+
+constexpr int PC = 1024;  // flat entries per chunk == threads per block
+
+__global__ void __launch_bounds__(PC)
+perm_count_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ chunk_counts,
+                  int* __restrict__ err)
+{
+    extern __shared__ int pc_hist[];
+    for (int i = threadIdx.x; i < E; i += PC) pc_hist[i] = 0;
+    __syncthreads();
+    const int idx = blockIdx.x * PC + threadIdx.x;
+    if (idx < n) {
+        int e = ids[idx];
+        if (e >= 0 && e < E)
+            atomicAdd(&pc_hist[e], 1);
+        else
+            atomicOr(err, MOE_DEV_BAD_EXPERT_ID);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += PC) chunk_counts[(size_t)blockIdx.x * E + i] = pc_hist[i];
+}
+
+// One block.  offsets[E+1]: expert row boundaries.  chunk_base[c][e]: first
+// permuted row of expert e's entries that live in chunk c.
+__global__ void __launch_bounds__(1024)
+perm_scan_kernel(const int32_t* __restrict__ chunk_counts, int nchunks, int E,
+                 int32_t* __restrict__ chunk_base, int32_t* __restrict__ offsets)
+{
+    extern __shared__ int ps_tot[];  // [E+1]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int s = 0;
+        for (int c = 0; c < nchunks; c++) s += chunk_counts[(size_t)c * E + e];
+        ps_tot[e] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int e = 0; e < E; e++) {
+            int c = ps_tot[e];
+            ps_tot[e] = run;
+            offsets[e] = run;
+            run += c;
+        }
+        offsets[E] = run;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = ps_tot[e];
+        for (int c = 0; c < nchunks; c++) {
+            chunk_base[(size_t)c * E + e] = run;
+            run += chunk_counts[(size_t)c * E + e];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(PC)
+perm_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
+                    const int32_t* __restrict__ chunk_base, int32_t* __restrict__ perm,
+                    int32_t* __restrict__ dest)
+{
+    extern __shared__ int sc_wcnt[];  // [32 warps][E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < 32 * E; i += PC) sc_wcnt[i] = 0;
+    __syncthreads();
+    const int idx = blockIdx.x * PC + threadIdx.x;
+    int e = -1;
+    if (idx < n) {
+        e = ids[idx];
+        if (e < 0 || e >= E) e = -1;  // reported by the count pass; skipped here
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+    if (e >= 0 && rank_in_warp == 0) sc_wcnt[warp * E + e] = __popc(same);
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += PC) {  // exclusive prefix over warps
+        int run = 0;
+        for (int w = 0; w < 32; w++) {
+            int c = sc_wcnt[w * E + ee];
+            sc_wcnt[w * E + ee] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    if (e >= 0) {
+        int pos = chunk_base[(size_t)blockIdx.x * E + e] + sc_wcnt[warp * E + e] + rank_in_warp;
+        perm[pos] = idx;
+        if (dest) dest[idx] = pos;
+    }
+}
+
+// xp[r, :] = x[perm[r] / K, :] for r < offsets[E]; one warp per row, 16-byte moves.
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
+                   const int32_t* __restrict__ offsets, int E, int K, int H, int rows_cap,
+                   __half* __restrict__ xp)
+{
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows_cap || r >= offsets[E]) return;
+    const int src_t = perm[r] / K;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)src_t * H);
+    uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)r * H);
+    const int nv = H >> 3;
+    for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+}
+
+cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
+                           int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,
+                           int* err, cudaStream_t s)
+{
+    const int nchunks = (n + PC - 1) / PC;
+    if (nchunks > 0) {
+        perm_count_kernel<<<nchunks, PC, E * sizeof(int), s>>>(ids, n, E, chunk_counts, err);
+    }
+    perm_scan_kernel<<<1, 1024, (E + 1) * sizeof(int), s>>>(chunk_counts, nchunks, E, chunk_base,
+                                                            offsets);
+    if (nchunks > 0) {
+        perm_scatter_kernel<<<nchunks, PC, 32 * E * sizeof(int), s>>>(ids, n, E, chunk_base, perm,
+                                                                      dest);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* offsets, int E,
+                               int K, int H, int rows_cap, __half* xp, cudaStream_t s)
+{
+    if (rows_cap == 0) return cudaSuccess;
+    gather_rows_kernel<<<(rows_cap + 7) / 8, 256, 0, s>>>(x, perm, offsets, E, K, H, rows_cap, xp);
+    return cudaGetLastError();
+}
+
+}  // namespace moe
