@@ -83,6 +83,23 @@ int MoeExpertFFN(const void* x, const int32_t* expert_ids, const void* weights,
 int MoeCombine(const void* expert_out, const int32_t* expert_ids, const void* weights, void* y,
                int64_t numTokens, int64_t hiddenSize, int64_t topK, void* stream);
 
+/* MoeExpertFFN for callers that cannot allocate device memory (a host framework
+ * that owns every allocation through its own pool, a runtime that forbids
+ * cudaMalloc after start-up, a service with a fixed memory budget).  This entry
+ * point has no counterpart in the reference.  The caller still passes inputs and
+ * outputs; the scratch is a static device array of MOE_NO_ALLOC_SCRATCH_BYTES
+ * inside the library, held by every GPU that loads it until the process exits.
+ * Problems whose MoeExpertFFNWorkspaceSize exceeds that limit are rejected with
+ * MOE_ERR_WORKSPACE_TOO_SMALL.  The first call on a device looks up the array's
+ * device address (make it before any stream capture).  All calls share the one
+ * array: calls that overlap on the GPU race and must be serialised by the caller.
+ * Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define MOE_NO_ALLOC_SCRATCH_BYTES (64u << 20)
+int MoeExpertFFNNoAlloc(const void* x, const int32_t* expert_ids, const void* weights,
+                        const void* expert_weights, void* expert_out, int64_t numTokens,
+                        int64_t hiddenSize, int64_t numExperts, int64_t topK,
+                        int64_t intermediateSize, void* stream);
+
 /* ------------------------------------------------------------------ whole layer */
 
 /* The three operators in sequence (the flow of tests/test_moe.cpp:446-463), with
