@@ -40,8 +40,9 @@ static RoutingPlan routing_plan(int H, int E)
 {
     RoutingPlan p;
     p.tpe = RT_THREADS / E;
-    p.P = (16 + p.tpe - 1) / p.tpe;
-    if (p.P > RT_MAXP) p.P = RT_MAXP;
+    int want = (16 + p.tpe - 1) / p.tpe;  // >= 16 tokens per block
+    p.P = 1;
+    while (p.P < want && p.P < RT_MAXP) p.P *= 2;
     p.TT = p.tpe * p.P;
     int hc = 16384 / E;
     if (16384 / p.TT < hc) hc = 16384 / p.TT;
@@ -55,10 +56,13 @@ static RoutingPlan routing_plan(int H, int E)
     return p;
 }
 
+// P (token chains per thread) is a template parameter so that the accumulators
+// are indexed statically and stay in registers.
+template <int P>
 __global__ void __launch_bounds__(RT_THREADS)
 routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_gate,
                     int32_t* __restrict__ expert_ids, __half* __restrict__ weights, int T, int H,
-                    int E, int K, int tpe, int P, int TT, int HC)
+                    int E, int K, int tpe, int TT, int HC)
 {
     extern __shared__ __align__(16) uint8_t rt_smem[];
     __half* xs = reinterpret_cast<__half*>(rt_smem);                  // [TT][HC]
@@ -72,9 +76,9 @@ routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_g
     const int e = tid % E;
     const int tslot = tid / E;
 
-    float acc[RT_MAXP];
+    float acc[P];
 #pragma unroll
-    for (int j = 0; j < RT_MAXP; j++) acc[j] = 0.0f;
+    for (int j = 0; j < P; j++) acc[j] = 0.0f;
 
     for (int h0 = 0; h0 < H; h0 += HC) {
         const int hc = min(HC, H - h0);  // multiple of 8 because H is
@@ -87,10 +91,11 @@ routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_g
             if (t < T) val = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + h0 + c));
             *reinterpret_cast<uint4*>(xs + (size_t)r * HC + c) = val;
         }
-        // stage w_gate chunk transposed: ws[e][h] = w_gate[h0+h][e]
+        // stage w_gate chunk transposed: ws[e][h] = w_gate[h0+h][e]; h-fastest so the
+        // shared-memory stores of a warp are consecutive (w_gate itself is L2-resident)
         for (int v = tid; v < hc * E; v += RT_THREADS) {
-            int h = v / E, ee = v - h * E;
-            ws[(size_t)ee * wstride + h] = w_gate[(size_t)(h0 + h) * E + ee];
+            int ee = v / hc, h = v - ee * hc;
+            ws[(size_t)ee * wstride + h] = __ldg(w_gate + (size_t)(h0 + h) * E + ee);
         }
         __syncthreads();
         if (active) {
@@ -106,8 +111,8 @@ routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_g
                     wf[2 * q + 1] = f.y;
                 }
 #pragma unroll
-                for (int j = 0; j < RT_MAXP; j++) {
-                    if (j < P) {
+                for (int j = 0; j < P; j++) {
+                    {
                         const int r = tslot + j * tpe;
                         uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)r * HC + h);
                         const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
@@ -127,8 +132,7 @@ routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_g
     }
     if (active) {
 #pragma unroll
-        for (int j = 0; j < RT_MAXP; j++)
-            if (j < P) lg[(size_t)(tslot + j * tpe) * E + e] = acc[j];
+        for (int j = 0; j < P; j++) lg[(size_t)(tslot + j * tpe) * E + e] = acc[j];
     }
     __syncthreads();
 
@@ -177,16 +181,21 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
 {
     if (T == 0) return cudaSuccess;
     RoutingPlan p = routing_plan(H, E);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(routing_topk_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
+    const int grid = (T + p.TT - 1) / p.TT;
+    switch (p.P) {
+#define MOE_ROUTING_CASE(PP)                                                                       \
+    case PP:                                                                                       \
+        routing_topk_kernel<PP><<<grid, RT_THREADS, p.smem, s>>>(x, w_gate, ids, weights, T, H, E, \
+                                                                 K, p.tpe, p.TT, p.HC);             \
+        break;
+        MOE_ROUTING_CASE(1)
+        MOE_ROUTING_CASE(2)
+        MOE_ROUTING_CASE(4)
+        MOE_ROUTING_CASE(8)
+        MOE_ROUTING_CASE(16)
+#undef MOE_ROUTING_CASE
+        default: return cudaErrorInvalidValue;
     }
-    int grid = (T + p.TT - 1) / p.TT;
-    routing_topk_kernel<<<grid, RT_THREADS, p.smem, s>>>(x, w_gate, ids, weights, T, H, E, K, p.tpe,
-                                                         p.P, p.TT, p.HC);
     return cudaGetLastError();
 }
 
