@@ -222,15 +222,35 @@ def run_ours(args):
     moe = __import__("_moe_loader").load()
     T, H, E, K, I, seed = moe.CONFIGS[args.config]
     dev = torch.device("cuda", local)
-    # every rank runs the layer on its own batch (per-GPU work fixed as N grows)
-    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed + rank, device=dev)
-    ws = torch.empty((moe.moe_layer_workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
+    # every rank routes its own batch of T tokens (per-GPU work fixed as N grows);
+    # the weights are one model (same seed on every rank)
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev)
+    if rank > 0:
+        x = moe.make_inputs_torch(T, H, 1, 1, 8, seed + rank, device=dev)[0]
     y = torch.empty((T, H), dtype=torch.float16, device=dev)
     flush = torch.empty((L2_FLUSH_BYTES,), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    ep = None
+    if world > 1:
+        # expert parallel: rank r keeps experts [r*E/N, (r+1)*E/N) and exchanges
+        # token rows with NCCL send/recv inside MoeEpLayerForward
+        if E % world:
+            raise SystemExit(f"E={E} is not divisible by {world} GPUs")
+        El = E // world
+        ew = ew[rank * El:(rank + 1) * El].contiguous()
+        torch.cuda.empty_cache()
+        uid = [moe.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ep = moe.EpContext(uid[0], rank, world, timeout_ms=120000)
+        ws = torch.empty((ep.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
 
-    def step():
-        moe.moe_layer_forward(x, wg, ew, K, y=y, workspace=ws)
+        def step(xin=None):
+            ep.forward(x if xin is None else xin, wg, ew, K, y=y, workspace=ws)
+    else:
+        ws = torch.empty((moe.moe_layer_workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
+
+        def step(xin=None):
+            moe.moe_layer_forward(x if xin is None else xin, wg, ew, K, y=y, workspace=ws)
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -272,7 +292,7 @@ def run_ours(args):
         if j >= 0:
             e_starts[j].record(stream)
         x_in.copy_(x_host, non_blocking=True)
-        moe.moe_layer_forward(x_in, wg, ew, K, y=y, workspace=ws)
+        step(x_in)
         y_host.copy_(y, non_blocking=True)
         if j >= 0:
             e_ends[j].record(stream)
@@ -306,7 +326,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I} per GPU",
-                       "global_batch": world * T, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "global_batch": world * T, "parallelism": f"ep{world} (expert parallel, NCCL send/recv)" if world > 1 else "single GPU",
                        "l2": "flushed between timed steps (512 MB write)", "inputs": "seeded N(0,1)/N(0,1/fan_in) fp16"},
             "roofline": {"kernel": "gemm_swiglu (gate/up grouped GEMM + SwiGLU epilogue)", "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
@@ -320,7 +340,7 @@ def run_ours(args):
                             "hbm_peak_gbs": hbm},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": args.steps * 8,
+            "gpu_launches": args.steps * (11 if world > 1 else 8),
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -329,6 +349,8 @@ def run_ours(args):
             except Exception as exc:  # reported, never fatal for the GPU number
                 line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
         print(json.dumps(line), flush=True)
+    if ep is not None:
+        ep.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -27,5 +27,8 @@ from .ops import (  # noqa: F401
     trace_start,
     trace_stop,
     TRACE_STAGES,
+    EpContext,
+    ep_unique_id,
+    ep_plan,
 )
 from .inputs import make_inputs, make_inputs_torch, CONFIGS  # noqa: F401

@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libmoe_b200.so")
 
-SOURCES = ["routing.cu", "permute.cu", "grouped_gemm.cu", "combine.cu", "moe_ops.cu", "no_alloc.cu"]
+SOURCES = ["routing.cu", "permute.cu", "grouped_gemm.cu", "combine.cu", "moe_ops.cu", "no_alloc.cu", "ep.cu"]
 HEADERS = ["moe_common.cuh", "moe_kernels.h"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -46,7 +46,7 @@ def build(verbose: bool = False) -> str:
                 print(" ".join(cmd), flush=True)
             subprocess.check_call(cmd)
     if _stale(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs]
+        cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs, "-lnccl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.check_call(cmd)

@@ -25,7 +25,7 @@
 // same time share one weight tile in L2 and every weight byte comes from HBM once.
 // The tile list is derived on the device from offsets[] (no host sync).
 //
-// No TMA multicast and no cluster launch are used: the same kernel runs on every
+// No cluster launch and no cluster-broadcast loads are used: the same kernel runs on every
 // rank of the expert-parallel path.
 #include "moe_common.cuh"
 #include "moe_kernels.h"

@@ -1,7 +1,7 @@
 // moe_common.cuh -- shared device helpers for the sm_100a MoE kernels.
 //
 // Thin inline-PTX wrappers for the Blackwell features the kernels use: mbarriers
-// with bounded waits, TMA tiled loads (no multicast anywhere in this library),
+// with bounded waits, TMA tiled loads (each CTA loads only into its own shared memory),
 // and the tcgen05 tensor-core path (TMEM allocation, UMMA issue, commit, TMEM
 // loads).  Every wait is bounded: after MOE_WAIT_LIMIT_NS of %globaltimer time it
 // records an error code in a device flag and returns false so the caller can

@@ -28,6 +28,17 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
                              const int32_t* perm, __half* expert_out, int* err, int rows_cap,
                              int H, int E, int I, int max_ctas, cudaStream_t s);
 
+cudaError_t launch_combine_indexed(const __half* rows, const int32_t* dest, const __half* weights,
+                                   __half* y, int T, int H, int K, cudaStream_t s);
+
+cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, int H, __half* dst,
+                             cudaStream_t s);
+
+// Stage tracing (MoeTraceStart/Stop): the event array of the call being traced
+// (nullptr when tracing is off) and a record at stage boundary `boundary` (0..6).
+cudaEvent_t* trace_begin_call();
+void trace_mark(cudaEvent_t* ev, int boundary, cudaStream_t s);
+
 cudaError_t launch_combine(const __half* expert_out, const __half* weights, __half* y, int T,
                            int H, int K, cudaStream_t s);
 

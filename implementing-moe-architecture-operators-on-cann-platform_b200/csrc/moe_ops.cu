@@ -14,9 +14,7 @@
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
-namespace {
-
-thread_local int g_last_cuda_error = 0;
+namespace moe {
 
 // ---- stage tracing: events[call][0..MOE_TRACE_STAGES] at stage boundaries
 struct Trace {
@@ -28,16 +26,26 @@ struct Trace {
 thread_local Trace g_trace;
 constexpr int kTraceEv = MOE_TRACE_STAGES + 1;
 
-// Returns the event array of the call being traced, or nullptr.
 cudaEvent_t* trace_begin_call()
 {
     if (!g_trace.on || g_trace.next >= g_trace.max_calls) return nullptr;
     return &g_trace.ev[(size_t)g_trace.next++ * kTraceEv];
 }
-inline void trace_mark(cudaEvent_t* ev, int boundary, cudaStream_t s)
+void trace_mark(cudaEvent_t* ev, int boundary, cudaStream_t s)
 {
     if (ev) cudaEventRecord(ev[boundary], s);
 }
+
+}  // namespace moe
+
+using moe::g_trace;
+using moe::kTraceEv;
+using moe::trace_begin_call;
+using moe::trace_mark;
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
 
 int cuda_status(cudaError_t e)
 {
@@ -189,7 +197,7 @@ int MoeRoutingTopK(const void* x, const void* w_gate, int32_t* expert_ids, void*
     if (!shapes_ok(T, H, E, K)) return MOE_ERR_BAD_SHAPE;
     if (T == 0) return MOE_OK;
     if (!x || !w_gate || !expert_ids || !weights) return MOE_ERR_NULL_POINTER;
-    if (!aligned16(x)) return MOE_ERR_MISALIGNED;
+    if (!aligned16(x) || !aligned16(w_gate)) return MOE_ERR_MISALIGNED;
     return cuda_status(moe::launch_routing(static_cast<const __half*>(x),
                                            static_cast<const __half*>(w_gate), expert_ids,
                                            static_cast<__half*>(weights), (int)T, (int)H, (int)E,
@@ -259,7 +267,7 @@ int MoeLayerForward(const void* x, const void* w_gate, const void* expert_weight
     if (!weights) weights = at<void>(workspace, L.weights);
     if (!expert_out) expert_out = at<void>(workspace, L.expert_out);
     if (!aligned16(workspace) ||
-        (T > 0 && (!aligned16(x) || !aligned16(expert_weights) || !aligned16(y) ||
+        (T > 0 && (!aligned16(x) || !aligned16(w_gate) || !aligned16(expert_weights) || !aligned16(y) ||
                    !aligned16(expert_out))))
         return MOE_ERR_MISALIGNED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -125,6 +125,28 @@ gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ per
     for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
 }
 
+// dst[r, :] = src[idx[r], :] for r < rows; one warp per row, 16-byte moves.
+__global__ void __launch_bounds__(256)
+copy_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ idx, int rows, int H,
+                 __half* __restrict__ dst)
+{
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + (size_t)idx[r] * H);
+    uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)r * H);
+    const int nv = H >> 3;
+    for (int v = lane; v < nv; v += 32) d4[v] = __ldg(s4 + v);
+}
+
+cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, int H, __half* dst,
+                             cudaStream_t s)
+{
+    if (rows == 0) return cudaSuccess;
+    copy_rows_kernel<<<(rows + 7) / 8, 256, 0, s>>>(src, idx, rows, H, dst);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
                            int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,
                            int* err, cudaStream_t s)

@@ -78,6 +78,14 @@ def lib():
         L.MoeStatusString.argtypes = [ctypes.c_int]
         L.MoeStatusString.restype = ctypes.c_char_p
         L.MoeLastCudaError.argtypes = []
+        L.MoeEpGetUniqueId.argtypes = [_vp]
+        L.MoeEpInit.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]
+        L.MoeEpDestroy.argtypes = [_vp]
+        L.MoeEpWorkspaceSize.argtypes = [ctypes.c_int] + [_i64] * 6
+        L.MoeEpWorkspaceSize.restype = _sz
+        L.MoeEpLayerForward.argtypes = [_vp] * 5 + [_i64] * 6 + [_vp, _sz, _vp]
+        _i32p = ctypes.POINTER(ctypes.c_int32)
+        L.MoeEpPlan.argtypes = [_i32p, _i32p, ctypes.c_int, ctypes.c_int, _i32p, _i32p, _i32p, _i32p]
         L.MoeTraceStart.argtypes = [ctypes.c_int]
         L.MoeTraceStop.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int, _intp]
         L.MoeRoutingInferShape.argtypes = [_i64p, ctypes.c_int, _i64p, ctypes.c_int, _i64, _i64p, _i64p,
@@ -293,3 +301,71 @@ def trace_stop(max_calls: int):
     for c in range(min(n.value, max_calls)):
         out.append({st: float(buf[c * len(TRACE_STAGES) + i]) for i, st in enumerate(TRACE_STAGES)})
     return out
+
+
+# ----------------------------------------------------------------------------- expert parallel
+EP_UNIQUE_ID_BYTES = 128
+
+
+def ep_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(EP_UNIQUE_ID_BYTES)
+    _check(lib().MoeEpGetUniqueId(buf), "MoeEpGetUniqueId")
+    return buf.raw
+
+
+def ep_plan(send_counts, recv_counts):
+    """MoeEpPlan on [n, El] int32 arrays -> (sendOff, recvOff, expertOff, segments[El*n, 3])."""
+    import numpy as np
+
+    sc = np.ascontiguousarray(send_counts, np.int32)
+    rc = np.ascontiguousarray(recv_counts, np.int32)
+    n, El = sc.shape
+    so = np.empty(n + 1, np.int32)
+    ro = np.empty(n + 1, np.int32)
+    eo = np.empty(El + 1, np.int32)
+    seg = np.empty((El * n, 3), np.int32)
+    p = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))  # noqa: E731
+    _check(lib().MoeEpPlan(p(sc), p(rc), n, El, p(so), p(ro), p(eo), p(seg)), "MoeEpPlan")
+    return so, ro, eo, seg
+
+
+class EpContext:
+    """One rank of the expert-parallel layer (MoeEpInit / MoeEpLayerForward)."""
+
+    def __init__(self, unique_id: bytes, rank: int, nranks: int, timeout_ms: int = 60000):
+        self.rank, self.nranks = rank, nranks
+        h = _vp()
+        _check(lib().MoeEpInit(ctypes.c_char_p(unique_id), rank, nranks, timeout_ms, ctypes.byref(h)), "MoeEpInit")
+        self.h = h
+        self._ws = None
+
+    def workspace_size(self, T, H, E, K, I, max_recv_rows=0):
+        return int(lib().MoeEpWorkspaceSize(self.nranks, T, H, E, K, I, max_recv_rows))
+
+    def forward(self, x, w_gate, expert_weights_local, topK=2, y=None, max_recv_rows=0, workspace=None):
+        torch = _torch()
+        _cuda(x, "x", torch.float16)
+        _cuda(w_gate, "w_gate", torch.float16)
+        _cuda(expert_weights_local, "expert_weights_local", torch.float16)
+        T, H = x.shape
+        E = w_gate.shape[1]
+        I = expert_weights_local.shape[1] // 3
+        if y is None:
+            y = torch.empty((T, H), dtype=torch.float16, device=x.device)
+        if workspace is None:
+            need = self.workspace_size(T, H, E, topK, I, max_recv_rows)
+            if need == 0:
+                raise MoeError(-2, "MoeEpWorkspaceSize")
+            if self._ws is None or self._ws.numel() < need:
+                self._ws = torch.empty((need,), dtype=torch.uint8, device=x.device)
+            workspace = self._ws
+        _check(lib().MoeEpLayerForward(self.h, _ptr(x), _ptr(w_gate), _ptr(expert_weights_local), _ptr(y), T, H,
+                                       E, topK, I, max_recv_rows, _ptr(workspace), workspace.numel(),
+                                       _stream_handle(x)), "MoeEpLayerForward")
+        return y
+
+    def close(self):
+        if self.h:
+            rc = lib().MoeEpDestroy(self.h)
+            self.h = None
+            _check(rc, "MoeEpDestroy")

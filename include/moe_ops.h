@@ -27,7 +27,7 @@
  * MoeGetDeviceError.
  *
  * Supported shapes: E in [1,256], K in [1, min(8,E)], H and I multiples of 8,
- * T*K < 2^31.  x, expert_weights, expert_out, y and the workspace must be
+ * T*K < 2^31.  x, w_gate, expert_weights, expert_out, y and the workspace must be
  * 16-byte aligned.
  */
 #ifndef MOE_OPS_H
@@ -113,6 +113,52 @@ int MoeLayerForward(const void* x, const void* w_gate, const void* expert_weight
                     int64_t intermediateSize, void* workspace, size_t workspaceBytes,
                     void* stream);
 
+/* ------------------------------------------------------------------ expert parallel
+ * The layer partitioned expert-parallel over n GPUs (one process or thread per
+ * GPU).  Rank r owns experts [r*E/n, (r+1)*E/n) -- a contiguous slice
+ * expert_weights_local [E/n, 3I, H] of the [E,3I,H] tensor -- and routes its own
+ * T tokens.  Token rows travel to their experts' owners and back with NCCL
+ * send/recv over NVLink.  The reference is single-device (tests/test_moe.cpp:642-648
+ * pins device 0); this has no counterpart there and follows the same operator
+ * semantics, so rank r's y equals MoeLayerForward on its tokens with all weights. */
+#define MOE_EP_UNIQUE_ID_BYTES 128
+typedef struct MoeEpContext MoeEpContext;
+
+/* Writes an NCCL unique id (MOE_EP_UNIQUE_ID_BYTES bytes); one rank calls it and
+ * the caller distributes the bytes to every rank. */
+int MoeEpGetUniqueId(void* uniqueId);
+
+/* Joins the communicator on the current CUDA device.  Non-blocking NCCL: every
+ * wait is bounded by timeoutMs (<= 0: 60 s); on timeout the communicator is
+ * aborted and MOE_ERR_TIMEOUT returned. */
+int MoeEpInit(const void* uniqueId, int rank, int nranks, int timeoutMs, MoeEpContext** ctx);
+int MoeEpDestroy(MoeEpContext* ctx);
+
+/* Workspace of MoeEpLayerForward.  maxRecvRows bounds the (token, slot) rows this
+ * rank's experts may receive in one call (<= 0: the worst case nranks*T*K). */
+size_t MoeEpWorkspaceSize(int nranks, int64_t numTokens, int64_t hiddenSize, int64_t numExperts,
+                          int64_t topK, int64_t intermediateSize, int64_t maxRecvRows);
+
+/* x [T,H] (this rank's tokens), w_gate [H,E] (all experts), expert_weights_local
+ * [E/n, 3I, H] -> y [T,H].  Synchronises the host once per call, on the exchanged
+ * row counts (bounded by the context's timeout).  Returns MOE_ERR_WORKSPACE_TOO_SMALL
+ * if more rows than maxRecvRows arrive (nothing is written past the workspace). */
+int MoeEpLayerForward(MoeEpContext* ctx, const void* x, const void* w_gate,
+                      const void* expert_weights_local, void* y, int64_t numTokens,
+                      int64_t hiddenSize, int64_t numExperts, int64_t topK,
+                      int64_t intermediateSize, int64_t maxRecvRows, void* workspace,
+                      size_t workspaceBytes, void* stream);
+
+/* The host-side exchange plan of one rank (pure host code).  sendCounts[r][e]: rows
+ * this rank sends to rank r for r's local expert e; recvCounts[s][e]: rows it
+ * receives from rank s for its local expert e (both [nranks][expertsPerRank]).
+ * Outputs: sendOff[nranks+1], recvOff[nranks+1] (row offsets of each peer's block),
+ * expertOff[expertsPerRank+1] (offsets after the expert-major reorder) and
+ * segments[expertsPerRank*nranks][3] = {dst row, src row, rows} for each
+ * (expert e, source s) at index e*nranks+s. */
+int MoeEpPlan(const int32_t* sendCounts, const int32_t* recvCounts, int nranks, int expertsPerRank,
+              int32_t* sendOff, int32_t* recvOff, int32_t* expertOff, int32_t* segments);
+
 /* ------------------------------------------------------------------ permutation */
 
 /* The token permutation inside MoeExpertFFN, exposed on its own.  Replaces the
@@ -137,8 +183,10 @@ int MoeGetDeviceError(const void* workspace, int* code, void* stream);
  * and MoeTraceStop, every MoeLayerForward / MoeExpertFFN call made on this host
  * thread records CUDA events at its stage boundaries on its stream, for up to
  * maxCalls calls.  MoeTraceStop synchronises on those events and writes, per
- * call, MOE_TRACE_STAGES durations in milliseconds (routing, permute, gather,
- * gate/up GEMM + SwiGLU, down GEMM, combine; stages a call does not run read 0). */
+ * call, MOE_TRACE_STAGES durations in milliseconds (routing, permute, gather (in
+ * MoeEpLayerForward: gather, count exchange, dispatch and reorder),
+ * gate/up GEMM + SwiGLU, down GEMM, combine (with the EP return exchange); stages a
+ * call does not run read 0).  MoeEpLayerForward calls are traced too. */
 #define MOE_TRACE_STAGES 6
 int MoeTraceStart(int maxCalls);
 int MoeTraceStop(float* stageMs, int maxCalls, int* numCalls);
