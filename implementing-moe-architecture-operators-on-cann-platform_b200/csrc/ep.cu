@@ -24,6 +24,7 @@
 // set-up, group completion, the counts event) polls against a deadline and aborts
 // the communicator on timeout, returning MOE_ERR_TIMEOUT instead of hanging.
 #include <nccl.h>
+#include <stddef.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -35,6 +36,7 @@
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
+struct EpPeersHost;
 struct MoeEpContext {
     ncclComm_t comm = nullptr;
     int rank = 0, nranks = 1, device = 0;
@@ -43,6 +45,14 @@ struct MoeEpContext {
     cudaEvent_t counts_ready = nullptr;
     int32_t* host = nullptr;  // pinned: offsets [E+1], recv counts [n*El], plan tables
     size_t host_ints = 0;
+    // peer-memory path (process-per-GPU, up to 8 ranks): IPC-shared inboxes
+    int p2p_state = 0;  // 0 not tried, 1 ready, -1 unavailable (NCCL path)
+    int64_t p2p_T = 0, p2p_H = 0, p2p_E = 0, p2p_K = 0, p2p_R = 0;
+    void* p2p_base = nullptr;      // this rank's allocation
+    void* p2p_peer[8] = {};        // opened peer allocations (p2p_peer[rank] = p2p_base)
+    void* p2p_dev_peers = nullptr; // device copy of the peer pointer table
+    size_t off_cnt = 0, off_rows = 0, off_ret = 0, off_flags = 0;
+    unsigned long long epoch = 0;
 };
 
 namespace {
@@ -77,7 +87,7 @@ int wait_comm(MoeEpContext* c, clk::time_point deadline)
             c->broken = true;
             return MOE_ERR_TIMEOUT;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        std::this_thread::yield();  // enqueue completes in microseconds: spin, do not sleep
     }
 }
 
@@ -100,7 +110,7 @@ int wait_event(MoeEpContext* c, cudaEvent_t ev, clk::time_point deadline)
             c->broken = true;
             return MOE_ERR_TIMEOUT;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(5));
+        std::this_thread::yield();
     }
 }
 
@@ -170,6 +180,236 @@ __global__ void ep_row_map_kernel(const int32_t* __restrict__ seg, int nseg, int
     }
 }
 
+
+// ============================================================================ peer-memory path
+// One allocation per rank, shared with the peers through CUDA IPC:
+//   cnt   [n][E] int32   row s: source s's per-expert row counts (written by s)
+//   rows  [R][H] fp16    rows for this rank's experts, expert-major (written by sources)
+//   ret   [T*K][H] fp16  this rank's rows back from their experts, in permuted order
+//   flags [8] u64        0: counts, 1: rows, 2: ret -- each source adds 1 per call;
+//                        4/5: local completion counters of the dispatch kernel (u32)
+// Every flag only grows, so "call number c is complete" is flag >= c * n.
+constexpr int EP_MAX_PEERS = 8;
+
+struct EpPeers {
+    int32_t* cnt[EP_MAX_PEERS];
+    __half* rows[EP_MAX_PEERS];
+    __half* ret[EP_MAX_PEERS];
+    unsigned long long* flags[EP_MAX_PEERS];
+    unsigned long long* ret_flag[EP_MAX_PEERS];  // &flags[p][2], for the GEMM2 signal
+};
+
+enum EpDevError { EP_ERR_WAIT_COUNTS = 64, EP_ERR_WAIT_ROWS = 128, EP_ERR_WAIT_RET = 256, EP_ERR_OVERFLOW = 512 };
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait (one thread) until *flag >= target; on timeout records `code`.
+__device__ bool ep_wait_flag(const unsigned long long* flag, unsigned long long target, int* err, int code)
+{
+    if (ld_acquire_sys(flag) >= target) return true;
+    const uint64_t t0 = moe::global_timer_ns();
+    for (;;) {
+        if (ld_acquire_sys(flag) >= target) return true;
+        if (moe::global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) {
+            atomicOr(err, code);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+// Writes this rank's per-expert counts into row `me` of every peer's cnt inbox,
+// then signals each peer's counts flag.
+__global__ void ep_p2p_counts_kernel(const EpPeers* __restrict__ peers, const int32_t* __restrict__ offsets, int E,
+                                     int me, int n)
+{
+    for (int p = 0; p < n; p++)
+        for (int e = threadIdx.x; e < E; e += blockDim.x) peers->cnt[p][me * E + e] = offsets[e + 1] - offsets[e];
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < n) {
+        __threadfence_system();
+        atomicAdd_system(&peers->flags[threadIdx.x][0], 1ull);
+    }
+}
+
+// Plan, on the device, once every source's counts are in: for each global expert e
+// the row in its owner's inbox where this rank's rows start (disp_base[e]); this
+// rank's expert-major offsets (expoff[El+1]) and, for each (local expert, source),
+// {first inbox row, rows, row index in the source's permuted order} (seg).
+__global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt, const unsigned long long* flags, int E, int El,
+                                   int me, int n, int R, unsigned long long target, int* err,
+                                   int32_t* __restrict__ disp_base, int32_t* __restrict__ expoff,
+                                   int32_t* __restrict__ seg, int32_t* __restrict__ overflow)
+{
+    __shared__ int ok;
+    __shared__ int over;
+    extern __shared__ int32_t pl_tot[];  // [E] rows per global expert over all sources
+    if (threadIdx.x == 0) {
+        ok = ep_wait_flag(&flags[0], target, err, EP_ERR_WAIT_COUNTS);
+        over = 0;
+    }
+    __syncthreads();
+    if (!ok) {  // counts never arrived: plan nothing, move nothing
+        for (int i = threadIdx.x; i <= El; i += blockDim.x) expoff[i] = 0;
+        for (int i = threadIdx.x; i < El * n; i += blockDim.x) seg[3 * i + 2] = 0;
+        if (threadIdx.x == 0) *overflow = 1;
+        return;
+    }
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int t = 0;
+        for (int s = 0; s < n; s++) t += cnt[s * E + e];
+        pl_tot[e] = t;
+    }
+    __syncthreads();
+    // per owner p: expert-major prefix over its experts; capacity check
+    for (int p = threadIdx.x; p < n; p += blockDim.x) {
+        long long run = 0;
+        for (int el = 0; el < El; el++) {
+            const int e = p * El + el;
+            long long before = 0;
+            for (int s = 0; s < me; s++) before += cnt[s * E + e];
+            disp_base[e] = (int32_t)(run + before);
+            if (p == me) expoff[el] = (int32_t)run;
+            run += pl_tot[e];
+        }
+        if (p == me) expoff[El] = (int32_t)run;
+        if (run > R) atomicOr(&over, 1);
+    }
+    __syncthreads();
+    if (over) {
+        if (threadIdx.x == 0) {
+            atomicOr(err, EP_ERR_OVERFLOW);
+            *overflow = 1;
+        }
+        for (int i = threadIdx.x; i <= El; i += blockDim.x) expoff[i] = 0;
+        for (int i = threadIdx.x; i < El * n; i += blockDim.x) seg[3 * i + 2] = 0;
+        return;
+    }
+    if (threadIdx.x == 0) *overflow = 0;
+    for (int i = threadIdx.x; i < El * n; i += blockDim.x) {
+        const int el = i / n, s = i - el * n;
+        const int e = me * El + el;
+        long long d0 = 0;
+        for (int s2 = 0; s2 < s; s2++) d0 += cnt[s2 * E + e];
+        long long rb = 0;
+        for (int e2 = 0; e2 < e; e2++) rb += cnt[s * E + e2];
+        seg[3 * i] = expoff[el] + (int32_t)d0;  // expoff written above by the same block
+        seg[3 * i + 1] = (int32_t)rb;
+        seg[3 * i + 2] = cnt[s * E + e];
+    }
+}
+
+// Fused gather + dispatch: row r of this rank's permuted order (expert e) goes from
+// x[perm[r]/K] straight to its owner's inbox row disp_base[e] + (r - offsets[e]),
+// over NVLink for remote owners.  The last block to finish signals every peer's
+// rows flag.
+__global__ void __launch_bounds__(256)
+ep_p2p_dispatch_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
+                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ disp_base,
+                       const int32_t* __restrict__ overflow, const EpPeers* __restrict__ peers, int TK, int E,
+                       int El, int K, int H, int n, unsigned int* done)
+{
+    const int lane = threadIdx.x & 31;
+    const int nv = H >> 3;
+    if (!*overflow) {
+        for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < TK; r += gridDim.x * 8) {
+            int lo = 0, hi = E;  // expert e with offsets[e] <= r < offsets[e+1]
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (offsets[mid] <= r) lo = mid; else hi = mid;
+            }
+            const int e = lo;
+            const int p = e / El;
+            const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(perm[r] / K) * H);
+            uint4* dst = reinterpret_cast<uint4*>(peers->rows[p] + (size_t)(disp_base[e] + r - offsets[e]) * H);
+            for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned int old = atomicAdd(done, 1u);
+        if (old == gridDim.x - 1) {
+            *reinterpret_cast<volatile unsigned int*>(done) = 0u;
+            __threadfence_system();
+            for (int p = 0; p < n; p++) atomicAdd_system(&peers->flags[p][1], 1ull);
+        }
+    }
+}
+
+// Destination of every inbox row after the down GEMM: the source rank's ret inbox,
+// at the row's index in that source's permuted order.
+__global__ void ep_p2p_rowptr_kernel(const int32_t* __restrict__ seg, int nseg, int n, int H,
+                                     const EpPeers* __restrict__ peers, unsigned long long* __restrict__ row_ptr)
+{
+    for (int i = blockIdx.x; i < nseg; i += gridDim.x) {
+        const int s = i % n;
+        const int d0 = seg[3 * i], rb = seg[3 * i + 1], len = seg[3 * i + 2];
+        __half* base = peers->ret[s];
+        for (int j = threadIdx.x; j < len; j += blockDim.x)
+            row_ptr[d0 + j] = reinterpret_cast<unsigned long long>(base + (size_t)(rb + j) * H);
+    }
+}
+
+// Waits (bounded) until every source's rows have landed in this rank's inbox.
+__global__ void ep_p2p_wait_kernel(const unsigned long long* flag, unsigned long long target, int* err, int code)
+{
+    if (threadIdx.x == 0) ep_wait_flag(flag, target, err, code);
+}
+
+// combine over the returned rows, after every expert owner has signalled them
+__global__ void __launch_bounds__(256)
+ep_p2p_combine_kernel(const __half* __restrict__ ret, const int32_t* __restrict__ dest,
+                      const __half* __restrict__ weights, __half* __restrict__ y, int T, int H, int K,
+                      const unsigned long long* flag, unsigned long long target, int* err)
+{
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = ep_wait_flag(flag, target, err, EP_ERR_WAIT_RET);
+    __syncthreads();
+    (void)ok;  // on timeout the rows are stale; the error word says so
+    const int vpr = H >> 3;
+    const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= (long long)T * vpr) return;
+    const int t = (int)(v / vpr);
+    const int c = (int)(v - (long long)t * vpr) << 3;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
+    for (int k = 0; k < K; k++) {
+        const float w = __half2float(weights[(size_t)t * K + k]);
+        const int r = dest[(size_t)t * K + k];
+        uint4 q = __ldcv(reinterpret_cast<const uint4*>(ret + (size_t)r * H + c));  // written by peers
+        const __half2* q2 = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float2 f = __half22float2(q2[i]);
+            acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
+            acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
+        }
+    }
+    uint4 o;
+    o.x = moe::pack_half2(acc[0], acc[1]);
+    o.y = moe::pack_half2(acc[2], acc[3]);
+    o.z = moe::pack_half2(acc[4], acc[5]);
+    o.w = moe::pack_half2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
+}
+
+}  // namespace
+
+namespace {
+void p2p_release(MoeEpContext* c);
+int p2p_setup(MoeEpContext* c, int64_t T, int64_t H, int64_t E, int64_t K, int64_t R, cudaStream_t s);
+int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* ewl, void* y, int64_t T,
+                int64_t H, int64_t E, int64_t K, int64_t I, int64_t R, void* ws, const EpLayout& L,
+                cudaStream_t s);
 }  // namespace
 
 extern "C" {
@@ -267,6 +507,7 @@ int MoeEpDestroy(MoeEpContext* c)
     }
     if (c->counts_ready) cudaEventDestroy(c->counts_ready);
     if (c->host) cudaFreeHost(c->host);
+    p2p_release(c);
     delete c;
     return rc;
 }
@@ -302,6 +543,14 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int El = (int)(E / n);
     const EpLayout L = ep_layout(n, T, H, E, K, I, R);
+    // peer-memory path: set up (collectively) on the first call and whenever the
+    // shapes change; every rank must call with the same shapes
+    if (n <= 8 && !getenv("MOE_EP_FORCE_NCCL") && c->p2p_state >= 0 &&
+        (c->p2p_state == 0 || c->p2p_T != T || c->p2p_H != H || c->p2p_E != E || c->p2p_K != K || c->p2p_R != R)) {
+        int src = p2p_setup(c, T, H, E, K, R, s);
+        if (src != MOE_OK) return src;
+    }
+    if (c->p2p_state == 1) return p2p_forward(c, x, w_gate, expert_weights_local, y, T, H, E, K, I, R, ws, L, s);
     const auto deadline = clk::now() + std::chrono::milliseconds(c->timeout_ms);
     int* err = at<int>(ws, L.err);
     int32_t* offsets = at<int32_t>(ws, L.offsets);
@@ -447,3 +696,207 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------- peer-memory host side
+namespace {
+
+void p2p_release(MoeEpContext* c)
+{
+    for (int p = 0; p < c->nranks && p < 8; p++)
+        if (c->p2p_peer[p] && c->p2p_peer[p] != c->p2p_base) cudaIpcCloseMemHandle(c->p2p_peer[p]);
+    for (auto& q : c->p2p_peer) q = nullptr;
+    if (c->p2p_base) cudaFree(c->p2p_base);
+    if (c->p2p_dev_peers) cudaFree(c->p2p_dev_peers);
+    c->p2p_base = nullptr;
+    c->p2p_dev_peers = nullptr;
+    c->p2p_state = 0;
+}
+
+// Collective: allocates and zeroes this rank's inboxes, exchanges IPC handles with
+// NCCL, opens the peers' allocations, agrees (all ranks) whether every step worked,
+// and ends with a barrier so no peer signals a flag before it is zeroed.
+int p2p_setup(MoeEpContext* c, int64_t T, int64_t H, int64_t E, int64_t K, int64_t R, cudaStream_t s)
+{
+    const auto deadline = clk::now() + std::chrono::milliseconds(c->timeout_ms);
+    const int n = c->nranks;
+    if (c->p2p_base) {  // shapes changed: the previous call's kernels must be done first
+        if (cudaDeviceSynchronize() != cudaSuccess) return MOE_ERR_CUDA;
+        p2p_release(c);
+    }
+    size_t o = 0;
+    c->off_cnt = o;
+    o += align_up(sizeof(int32_t) * n * E);
+    c->off_flags = o;
+    o += align_up(64);
+    c->off_rows = o;
+    o += align_up((size_t)R * H * 2);
+    c->off_ret = o;
+    o += align_up((size_t)(T * K > 0 ? T * K : 1) * H * 2);
+    int ok = 1;
+    cudaIpcMemHandle_t mine;
+    memset(&mine, 0, sizeof(mine));
+    if (cudaMalloc(&c->p2p_base, o) != cudaSuccess) {
+        c->p2p_base = nullptr;
+        ok = 0;
+    }
+    if (ok && (cudaMemset(c->p2p_base, 0, o) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+               cudaIpcGetMemHandle(&mine, c->p2p_base) != cudaSuccess))
+        ok = 0;
+    cudaGetLastError();
+    // all-gather of the handles (and of `ok`) through NCCL
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t* d_h = nullptr;
+    int* d_ok = nullptr;
+    if (cudaMalloc(&d_h, hb * n) != cudaSuccess || cudaMalloc(&d_ok, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+    cudaMemcpy(d_h + hb * c->rank, &mine, hb, cudaMemcpyHostToDevice);
+    cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+    int rc = check_nccl(c, ncclGroupStart());
+    if (rc == MOE_OK) rc = check_nccl(c, ncclAllGather(d_h + hb * c->rank, d_h, hb, ncclUint8, c->comm, s));
+    if (rc == MOE_OK) rc = check_nccl(c, ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, c->comm, s));
+    if (rc == MOE_OK) rc = check_nccl(c, ncclGroupEnd());
+    if (rc == MOE_OK) rc = wait_comm(c, deadline);
+    if (rc == MOE_OK && cudaEventRecord(c->counts_ready, s) != cudaSuccess) rc = MOE_ERR_CUDA;
+    if (rc == MOE_OK) rc = wait_event(c, c->counts_ready, deadline);
+    std::vector<uint8_t> handles(hb * n);
+    if (rc == MOE_OK) {
+        cudaMemcpy(handles.data(), d_h, hb * n, cudaMemcpyDeviceToHost);
+        cudaMemcpy(&ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
+    }
+    if (rc != MOE_OK) {
+        cudaFree(d_h);
+        cudaFree(d_ok);
+        return rc;
+    }
+    // open the peers' allocations; then agree again on success
+    int opened = ok;
+    for (int p = 0; opened && p < n; p++) {
+        if (p == c->rank) {
+            c->p2p_peer[p] = c->p2p_base;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles.data() + hb * p, hb);
+        if (cudaIpcOpenMemHandle(&c->p2p_peer[p], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            c->p2p_peer[p] = nullptr;
+            opened = 0;
+        }
+    }
+    cudaGetLastError();
+    cudaMemcpy(d_ok, &opened, sizeof(int), cudaMemcpyHostToDevice);
+    rc = check_nccl(c, ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, c->comm, s));
+    if (rc == MOE_OK) rc = wait_comm(c, deadline);
+    if (rc == MOE_OK && cudaEventRecord(c->counts_ready, s) != cudaSuccess) rc = MOE_ERR_CUDA;
+    if (rc == MOE_OK) rc = wait_event(c, c->counts_ready, deadline);
+    if (rc == MOE_OK) cudaMemcpy(&opened, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    cudaFree(d_ok);
+    if (rc != MOE_OK) return rc;
+    if (!opened) {
+        p2p_release(c);
+        c->p2p_state = -1;  // every rank falls back to the NCCL path together
+        return MOE_OK;
+    }
+    EpPeers hp;
+    memset(&hp, 0, sizeof(hp));
+    for (int p = 0; p < n; p++) {
+        uint8_t* b = static_cast<uint8_t*>(c->p2p_peer[p]);
+        hp.cnt[p] = reinterpret_cast<int32_t*>(b + c->off_cnt);
+        hp.rows[p] = reinterpret_cast<__half*>(b + c->off_rows);
+        hp.ret[p] = reinterpret_cast<__half*>(b + c->off_ret);
+        hp.flags[p] = reinterpret_cast<unsigned long long*>(b + c->off_flags);
+        hp.ret_flag[p] = hp.flags[p] + 2;
+    }
+    if (cudaMalloc(&c->p2p_dev_peers, sizeof(EpPeers)) != cudaSuccess ||
+        cudaMemcpy(c->p2p_dev_peers, &hp, sizeof(hp), cudaMemcpyHostToDevice) != cudaSuccess)
+        return MOE_ERR_CUDA;
+    c->p2p_T = T;
+    c->p2p_H = H;
+    c->p2p_E = E;
+    c->p2p_K = K;
+    c->p2p_R = R;
+    c->epoch = 0;
+    c->p2p_state = 1;
+    return MOE_OK;
+}
+
+}  // namespace
+
+namespace {
+
+int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* ewl, void* y, int64_t T,
+                int64_t H, int64_t E, int64_t K, int64_t I, int64_t R, void* ws, const EpLayout& L,
+                cudaStream_t s)
+{
+    const int n = c->nranks, me = c->rank, El = (int)(E / n);
+    const int TK = (int)(T * K);
+    const unsigned long long target = (++c->epoch) * (unsigned long long)n;
+    const EpPeers* dp = static_cast<const EpPeers*>(c->p2p_dev_peers);
+    uint8_t* base = static_cast<uint8_t*>(c->p2p_base);
+    const int32_t* cnt_local = reinterpret_cast<const int32_t*>(base + c->off_cnt);
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(base + c->off_flags);
+    const __half* rows_local = reinterpret_cast<const __half*>(base + c->off_rows);
+    const __half* ret_local = reinterpret_cast<const __half*>(base + c->off_ret);
+    int* err = at<int>(ws, L.err);
+    int32_t* offsets = at<int32_t>(ws, L.offsets);
+    int32_t* perm = at<int32_t>(ws, L.perm);
+    int32_t* dest = at<int32_t>(ws, L.dest);
+    int32_t* ids = at<int32_t>(ws, L.ids);
+    __half* wts = at<__half>(ws, L.weights);
+    int32_t* disp_base = at<int32_t>(ws, L.sendcnt);  // [E]
+    int32_t* overflow = at<int32_t>(ws, L.recvcnt);   // [1]
+    int32_t* expoff = at<int32_t>(ws, L.expoff);
+    int32_t* seg = at<int32_t>(ws, L.seg);
+    unsigned long long* row_ptr = at<unsigned long long>(ws, L.xr);  // R entries fit: H*2 >= 8
+    __half* hbuf = at<__half>(ws, L.h);
+    unsigned int* done1 = reinterpret_cast<unsigned int*>(flags + 4);
+    unsigned int* done2 = reinterpret_cast<unsigned int*>(flags + 5);
+    cudaEvent_t* ev = moe::trace_begin_call();
+    moe::trace_mark(ev, 0, s);
+    if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return MOE_ERR_CUDA;
+    if (T > 0 && moe::launch_routing(static_cast<const __half*>(x), static_cast<const __half*>(w_gate), ids, wts,
+                                     (int)T, (int)H, (int)E, (int)K, s) != cudaSuccess)
+        return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 1, s);
+    if (moe::launch_permute(ids, TK, (int)E, at<int32_t>(ws, L.chunk_counts), at<int32_t>(ws, L.chunk_base),
+                            offsets, perm, dest, err, s) != cudaSuccess)
+        return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 2, s);
+    ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n);
+    ep_p2p_plan_kernel<<<1, 256, sizeof(int32_t) * E, s>>>(cnt_local, flags, (int)E, El, me, n, (int)R, target, err,
+                                                           disp_base, expoff, seg, overflow);
+    int dgrid = (TK + 7) / 8;
+    if (dgrid > 148 * 8) dgrid = 148 * 8;
+    if (dgrid < 1) dgrid = 1;
+    ep_p2p_dispatch_kernel<<<dgrid, 256, 0, s>>>(static_cast<const __half*>(x), perm, offsets, disp_base, overflow, dp,
+                                                 TK, (int)E, El, (int)K, (int)H, n, done1);
+    ep_p2p_rowptr_kernel<<<El * n < 1024 ? El * n : 1024, 256, 0, s>>>(seg, El * n, n, (int)H, dp, row_ptr);
+    ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 1, target, err, EP_ERR_WAIT_ROWS);
+    if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 3, s);
+    cudaError_t e = moe::launch_gemm_swiglu(rows_local, static_cast<const __half*>(ewl), expoff, hbuf, err, (int)R,
+                                            (int)H, El, (int)I, 0, s);
+    if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
+    if (e != cudaSuccess) return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 4, s);
+    // the down GEMM stores each row straight into its source rank's ret inbox and,
+    // when the launch is done, bumps every rank's ret flag
+    e = moe::launch_gemm_down_ptr(hbuf, static_cast<const __half*>(ewl), expoff, row_ptr, done2,
+                                  reinterpret_cast<unsigned long long* const*>(
+                                      reinterpret_cast<const uint8_t*>(dp) + offsetof(EpPeers, ret_flag)),
+                                  n, err, (int)R, (int)H, El, (int)I, s);
+    if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
+    if (e != cudaSuccess) return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 5, s);
+    const long long nv = (long long)T * (H >> 3);
+    if (nv > 0) {
+        ep_p2p_combine_kernel<<<(int)((nv + 255) / 256), 256, 0, s>>>(ret_local, dest, wts, static_cast<__half*>(y),
+                                                                     (int)T, (int)H, (int)K, flags + 2, target, err);
+    } else {
+        ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 2, target, err, EP_ERR_WAIT_RET);
+    }
+    if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+    moe::trace_mark(ev, 6, s);
+    return MOE_OK;
+}
+
+}  // namespace

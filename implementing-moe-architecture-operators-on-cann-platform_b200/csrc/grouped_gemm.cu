@@ -57,6 +57,14 @@ struct GemmArgs {
     int b_nstep;             // B rows advanced per N tile: 128 (GEMM1) or 256 (GEMM2)
     int b_hi_delta;          // row distance of the second B box: I (up rows) or 128
     int out_ld;              // leading dimension of out: I or H
+    // MODE_DOWN_PTR only: row r of the tile list goes to row_ptr[r] (a local or a
+    // peer GPU's address); when every CTA is done, the last one adds 1 to each
+    // *peer_flags[p] (system-scope release) so the owners of those rows know the
+    // rows have landed.
+    const unsigned long long* row_ptr;
+    unsigned int* done_counter;
+    unsigned long long* const* peer_flags;
+    int npeers;
 };
 
 struct GemmSmemTail {
@@ -284,7 +292,12 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             } else {
                 const int col0 = nt * GM_BN;
                 __half* dst = nullptr;
-                if (valid) dst = args.out + (size_t)args.perm[row0 + r] * args.out_ld + col0;
+                if (valid) {
+                    if (MODE == MODE_DOWN_PTR)
+                        dst = reinterpret_cast<__half*>(args.row_ptr[row0 + r]) + col0;
+                    else
+                        dst = args.out + (size_t)args.perm[row0 + r] * args.out_ld + col0;
+                }
 #pragma unroll 1
                 for (int j = 0; j < 8; j++) {
                     uint32_t v32[32];
@@ -311,11 +324,21 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
     }
 
+    if (MODE == MODE_DOWN_PTR) __threadfence_system();  // this thread's (peer) row stores
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, GM_TMEM_COLS);
+    }
+    if (MODE == MODE_DOWN_PTR && threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned int old = atomicAdd(args.done_counter, 1u);
+        if (old == gridDim.x - 1) {  // last CTA: every row of this launch is stored
+            *reinterpret_cast<volatile unsigned int*>(args.done_counter) = 0u;
+            __threadfence_system();
+            for (int p = 0; p < args.npeers; p++) atomicAdd_system(args.peer_flags[p], 1ull);
+        }
     }
 }
 
@@ -400,7 +423,7 @@ cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, c
         return cudaErrorInvalidValue;
     cudaError_t e = set_gemm_attr<MODE_SWIGLU>();
     if (e != cudaSuccess) return e;
-    GemmArgs a;
+    GemmArgs a = {};
     a.offsets = offsets;
     a.perm = nullptr;
     a.out = h;
@@ -430,7 +453,7 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
         return cudaErrorInvalidValue;
     cudaError_t e = set_gemm_attr<MODE_DOWN>();
     if (e != cudaSuccess) return e;
-    GemmArgs a;
+    GemmArgs a = {};
     a.offsets = offsets;
     a.perm = perm;
     a.out = expert_out;
@@ -446,6 +469,44 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
     a.out_ld = H;
     const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
     ffn_gemm_kernel<MODE_DOWN><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
+    return cudaGetLastError();
+}
+
+}  // namespace moe
+
+namespace moe {
+
+// GEMM2 with a per-row destination pointer table and a completion signal to peers
+// (the expert-parallel return path: rows go straight into the source ranks' memory).
+cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, const int32_t* offsets,
+                                 const unsigned long long* row_ptr, unsigned int* done_counter,
+                                 unsigned long long* const* peer_flags, int npeers, int* err, int rows_cap,
+                                 int H, int E, int I, cudaStream_t s)
+{
+    CUtensorMap ta, tb;
+    if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
+        !make_tmap(&tb, expert_weights, (uint64_t)I, (uint64_t)E * 3 * H))
+        return cudaErrorInvalidValue;
+    cudaError_t e = set_gemm_attr<MODE_DOWN_PTR>();
+    if (e != cudaSuccess) return e;
+    GemmArgs a = {};
+    a.offsets = offsets;
+    a.err = err;
+    a.E = E;
+    a.kdim = I;
+    a.nvalid = H;
+    a.n_tiles = (H + GM_BN - 1) / GM_BN;
+    a.b_rows_per_expert = 3 * H;
+    a.b_seg = 2 * H;
+    a.b_nstep = GM_BN;
+    a.b_hi_delta = 128;
+    a.out_ld = H;
+    a.row_ptr = row_ptr;
+    a.done_counter = done_counter;
+    a.peer_flags = peer_flags;
+    a.npeers = npeers;
+    const int grid = grid_for(rows_cap, E, a.n_tiles, 0);
+    ffn_gemm_kernel<MODE_DOWN_PTR><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
     return cudaGetLastError();
 }
 

@@ -8,7 +8,7 @@
 
 namespace moe {
 
-enum GemmMode { MODE_SWIGLU = 0, MODE_DOWN = 1 };
+enum GemmMode { MODE_SWIGLU = 0, MODE_DOWN = 1, MODE_DOWN_PTR = 2 };
 
 cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights,
                            int T, int H, int E, int K, cudaStream_t s);
@@ -38,6 +38,11 @@ cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, in
 // (nullptr when tracing is off) and a record at stage boundary `boundary` (0..6).
 cudaEvent_t* trace_begin_call();
 void trace_mark(cudaEvent_t* ev, int boundary, cudaStream_t s);
+
+cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, const int32_t* offsets,
+                                 const unsigned long long* row_ptr, unsigned int* done_counter,
+                                 unsigned long long* const* peer_flags, int npeers, int* err, int rows_cap,
+                                 int H, int E, int I, cudaStream_t s);
 
 cudaError_t launch_combine(const __half* expert_out, const __half* weights, __half* y, int T,
                            int H, int K, cudaStream_t s);

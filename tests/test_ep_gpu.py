@@ -25,16 +25,28 @@ def _need_gpu():
 SHAPES = [(300, 256, 8, 2, 512), (257, 512, 16, 2, 384)]
 
 
+@pytest.fixture(params=["p2p", "nccl"])
+def ep_path(request, monkeypatch):
+    """The peer-memory exchange (default) and the NCCL send/recv fallback."""
+    if request.param == "nccl":
+        monkeypatch.setenv("MOE_EP_FORCE_NCCL", "1")
+    else:
+        monkeypatch.delenv("MOE_EP_FORCE_NCCL", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("shape", SHAPES)
-def test_ep_single_rank_matches_layer(moe, shape):
+def test_ep_single_rank_matches_layer(moe, shape, ep_path):
     T, H, E, K, I = shape
     x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, 5)
     ref = moe.moe_layer_forward(x, wg, ew, K)
     ctx = moe.EpContext(moe.ep_unique_id(), 0, 1, timeout_ms=20000)
     try:
-        y = ctx.forward(x, wg, ew, K)
-        y2 = ctx.forward(x, wg, ew, K)  # a second call reuses the workspace
+        ws = torch.empty((ctx.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device="cuda")
+        y = ctx.forward(x, wg, ew, K, workspace=ws)
+        y2 = ctx.forward(x, wg, ew, K, workspace=ws)  # a second call reuses the workspace
         torch.cuda.synchronize()
+        assert moe.device_error(ws) == 0
     finally:
         ctx.close()
     assert torch.equal(y, ref) and torch.equal(y2, ref)
@@ -72,7 +84,7 @@ def _free_port():
     return p
 
 
-def _ep_rank(rank, n, port, shape, q):
+def _ep_rank(rank, n, port, shape, path, q):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -81,6 +93,8 @@ def _ep_rank(rank, n, port, shape, q):
     from _moe_loader import load
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if path == "nccl":
+        os.environ["MOE_EP_FORCE_NCCL"] = "1"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=n)
     moe = load()
@@ -95,9 +109,11 @@ def _ep_rank(rank, n, port, shape, q):
         ctx = moe.EpContext(uid[0], rank, n, timeout_ms=30000)
         try:
             local = ew[rank * El:(rank + 1) * El].contiguous()
-            y = ctx.forward(x, wg, local, K)
-            y2 = ctx.forward(x, wg, local, K)
+            ws = torch.empty((ctx.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device="cuda")
+            y = ctx.forward(x, wg, local, K, workspace=ws)
+            y2 = ctx.forward(x, wg, local, K, workspace=ws)
             torch.cuda.synchronize()
+            assert moe.device_error(ws) == 0
         finally:
             ctx.close()
         q.put((rank, bool(torch.equal(y, ref)), bool(torch.equal(y2, ref)), float((y.float() - ref.float()).abs().max())))
@@ -105,8 +121,9 @@ def _ep_rank(rank, n, port, shape, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("path", ["p2p", "nccl"])
 @pytest.mark.parametrize("shape", [(300, 256, 8, 2, 512), (1024, 2048, 16, 2, 1024)])
-def test_ep_multi_gpu_matches_layer(shape):
+def test_ep_multi_gpu_matches_layer(shape, path):
     n = min(torch.cuda.device_count(), 4)
     if n < 2:
         pytest.skip("needs 2 GPUs")
@@ -117,7 +134,7 @@ def test_ep_multi_gpu_matches_layer(shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, n, port, shape, q)) for r in range(n)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, n, port, shape, path, q)) for r in range(n)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(n)]
