@@ -32,3 +32,10 @@ from .ops import (  # noqa: F401
     ep_plan,
 )
 from .inputs import make_inputs, make_inputs_torch, CONFIGS  # noqa: F401
+
+
+def register_torch_ops():
+    """Registers torch.ops.moe_b200.* (routing_topk, expert_ffn, combine, layer_forward)."""
+    from . import torch_ops  # noqa: F401
+
+    return torch_ops

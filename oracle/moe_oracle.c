@@ -231,3 +231,16 @@ void oracle_moe_naive(const float* x, const float* w_gate, const float* ew, int 
     if (!ids_out) free(ids);
     if (!weights_out) free(w);
 }
+
+/*
+ * Inputs of the reference's NPU end-to-end test (tests/test_moe.cpp:373-381):
+ * srand(seed), then x, w_gate and expert_weights filled in that order with
+ * rand()/RAND_MAX*2-1 (uniform [-1,1]) from the C library's generator.
+ */
+void oracle_test_moe_inputs(unsigned seed, float* x, size_t nx, float* wg, size_t nwg, float* ew, size_t new_)
+{
+    srand(seed);
+    for (size_t i = 0; i < nx; i++) x[i] = (rand() / (float)RAND_MAX) * 2.0f - 1.0f;
+    for (size_t i = 0; i < nwg; i++) wg[i] = (rand() / (float)RAND_MAX) * 2.0f - 1.0f;
+    for (size_t i = 0; i < new_; i++) ew[i] = (rand() / (float)RAND_MAX) * 2.0f - 1.0f;
+}

@@ -58,6 +58,8 @@ def lib():
         L.oracle_permute.restype = _c_int
         L.oracle_expert_ffn.argtypes = [_f32p, _f32p, _i32p] + [_c_int] * 5 + [_f32p, _c_int]
         L.oracle_combine.argtypes = [_f32p, _f32p, _c_int, _c_int, _c_int, _f32p]
+        L.oracle_test_moe_inputs.argtypes = [ctypes.c_uint, _f32p, ctypes.c_size_t, _f32p, ctypes.c_size_t, _f32p,
+                                             ctypes.c_size_t]
         L.oracle_moe_naive.argtypes = [_f32p, _f32p, _f32p] + [_c_int] * 5 + [_f32p, _i32p, _f32p, _c_int]
         _lib = L
     return _lib
@@ -154,6 +156,16 @@ def moe_naive(x, w_gate, ew, K, nthreads=None):
                            ids.ctypes.data_as(_i32p), wts.ctypes.data_as(_f32p),
                            nthreads or os.cpu_count() or 1)
     return y, ids, wts
+
+
+def test_moe_inputs(T, H, E, I, seed=42):
+    """fp32 inputs of tests/test_moe.cpp:373-381 (srand(seed), uniform [-1,1], x, w_gate, weights)."""
+    x = np.empty((T, H), np.float32)
+    wg = np.empty((H, E), np.float32)
+    ew = np.empty((E, 3 * I, H), np.float32)
+    lib().oracle_test_moe_inputs(seed, x.ctypes.data_as(_f32p), x.size, wg.ctypes.data_as(_f32p), wg.size,
+                                 ew.ctypes.data_as(_f32p), ew.size)
+    return x, wg, ew
 
 
 # ----------------------------------------------------------------------------- reference itself
