@@ -22,6 +22,18 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"] if os.environ.get("MOE_PTXAS_VERBOSE") else \
         ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
+# extra compile definitions, e.g. MOE_NVCC_EXTRA="-DMOE_GEMM_STAGES=3" (tuning builds)
+FLAGS = FLAGS + os.environ.get("MOE_NVCC_EXTRA", "").split()
+
+
+STAMP = os.path.join(BUILD, "flags.txt")
+
+
+def _flags_changed() -> bool:
+    """True when the objects were built with other flags (e.g. a tuning build)."""
+    want = " ".join([NVCC, *ARCH, *FLAGS])
+    have = open(STAMP).read() if os.path.exists(STAMP) else None
+    return have != want
 
 
 def _stale(out: str, deps: list[str]) -> bool:
@@ -35,17 +47,20 @@ def build(verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     include = os.path.join(os.path.dirname(HERE), "include")
     hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(include, "moe_ops.h")]
+    force = _flags_changed()
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(BUILD, src.replace(".cu", ".o"))
         objs.append(o)
-        if _stale(o, [s] + hdrs):
+        if force or _stale(o, [s] + hdrs):
             cmd = [NVCC, *ARCH, *FLAGS, "-I", include, "-c", s, "-o", o]
             if verbose:
                 print(" ".join(cmd), flush=True)
             subprocess.check_call(cmd)
-    if _stale(LIB, objs):
+    with open(STAMP, "w") as f:
+        f.write(" ".join([NVCC, *ARCH, *FLAGS]))
+    if force or _stale(LIB, objs):
         cmd = [NVCC, *ARCH, "-shared", "-cudart", "shared", "-o", LIB, *objs, "-lnccl"]
         if verbose:
             print(" ".join(cmd), flush=True)

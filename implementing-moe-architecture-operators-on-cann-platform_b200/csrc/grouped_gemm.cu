@@ -35,7 +35,20 @@ namespace moe {
 constexpr int GM_BM = 128;        // rows per tile (UMMA M)
 constexpr int GM_BN = 256;        // accumulator columns per tile (UMMA N)
 constexpr int GM_BK = 64;         // k per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int GM_STAGES = 4;
+#ifndef MOE_GEMM_STAGES
+#define MOE_GEMM_STAGES 4
+#endif
+constexpr int GM_STAGES = MOE_GEMM_STAGES;
+#ifndef MOE_GEMM_ACCURATE_SILU
+#define MOE_GEMM_ACCURATE_SILU 0
+#endif
+#ifndef MOE_GEMM_EPI_DIRECT
+#define MOE_GEMM_EPI_DIRECT 0
+#endif
+#ifndef MOE_GEMM_NOSTORE
+#define MOE_GEMM_NOSTORE 0  // tuning builds only: 1 drops the epilogue's stores
+#endif
+
 constexpr int GM_A_BYTES = GM_BM * GM_BK * 2;          // 16 KB
 constexpr int GM_BHALF_BYTES = 128 * GM_BK * 2;        // 16 KB
 constexpr int GM_STAGE_BYTES = GM_A_BYTES + 2 * GM_BHALF_BYTES;  // 48 KB
@@ -78,9 +91,49 @@ struct GemmSmemTail {
     int tile_prefix[GM_MAX_E + 1];
 };
 
+// Epilogue staging for coalesced stores: per epilogue warp 32 rows x 80 bytes
+// (one 32-column fp16 chunk per row, padded by 16 bytes).
+constexpr int GM_STG_ROW = 80;
+constexpr int GM_STG_BYTES = 4 * 32 * GM_STG_ROW;
+
 __host__ __device__ constexpr size_t gemm_smem_bytes()
 {
-    return 1024 + (size_t)GM_STAGES * GM_STAGE_BYTES + sizeof(GemmSmemTail);
+    return 1024 + (size_t)GM_STAGES * GM_STAGE_BYTES + ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) +
+           GM_STG_BYTES;
+}
+
+// Stores one 32-column chunk (64 bytes) of each of the warp's 32 rows.  Each
+// thread parks its row's chunk in shared memory (rows padded to 80 bytes so the
+// 16-byte pieces of different rows fall in different banks); the warp then reads
+// it back transposed so that every store instruction writes 8 whole 64-byte row
+// segments (lane l: row 8i + l/4, piece l%4) instead of 32 scattered 16-byte ones.
+// dst: this thread's row destination for the chunk (nullptr: row not stored);
+// nbytes: valid bytes of the chunk (a multiple of 16), the same for every row.
+__device__ __forceinline__ void epi_warp_store(uint8_t* stg_warp, int lane, const uint4 (&v)[4], __half* dst,
+                                               int nbytes)
+{
+#if MOE_GEMM_EPI_DIRECT  // tuning builds: each thread stores its own row's pieces
+    if (dst)
+        for (int p = 0; p < 4; p++)
+            if (p * 16 < nbytes) reinterpret_cast<uint4*>(dst)[p] = v[p];
+    return;
+#endif
+    uint4* mine = reinterpret_cast<uint4*>(stg_warp + lane * GM_STG_ROW);
+    mine[0] = v[0];
+    mine[1] = v[1];
+    mine[2] = v[2];
+    mine[3] = v[3];
+    __syncwarp();
+    const int piece = lane & 3;
+    const unsigned long long d = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int row = 8 * i + (lane >> 2);
+        const unsigned long long rd = __shfl_sync(0xffffffffu, d, row);
+        const uint4 val = *reinterpret_cast<const uint4*>(stg_warp + row * GM_STG_ROW + piece * 16);
+        if (rd != 0ull && piece * 16 < nbytes) *reinterpret_cast<uint4*>(rd + piece * 16) = val;
+    }
+    __syncwarp();
 }
 
 // Maps a CTA-visited tile index to (expert, m tile, n tile).  Tile indices a
@@ -160,7 +213,11 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
             const uint64_t pol_a = l2_policy_evict_last();  // activations: reused by every N tile
-            const uint64_t pol_b = l2_policy_evict_first(); // weights: read by the m tiles in flight
+#ifndef MOE_GEMM_B_EVICT_FIRST
+            const uint64_t pol_b = l2_policy_evict_last();  // weights: shared by the m tiles in flight
+#else
+            const uint64_t pol_b = l2_policy_evict_first();
+#endif
             TileCursor cur;
             uint32_t it = 0;
             bool ok = true;
@@ -247,6 +304,8 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const int q = warp & 3;            // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;       // row inside the tile
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        uint8_t* stg_warp = smem + GM_STAGES * GM_STAGE_BYTES + ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) +
+                            (size_t)(warp - 2) * 32 * GM_STG_ROW;
         TileCursor cur;
         uint32_t lt = 0;
         for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
@@ -270,23 +329,31 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     tmem_ld_32x32b_x32(tbase + j * 32, g);
                     tmem_ld_32x32b_x32(tbase + 128 + j * 32, u);
                     tmem_ld_wait();
-                    if (valid) {
+                    {
                         uint32_t pk[16];
 #pragma unroll
                         for (int c = 0; c < 16; c++) {
                             const float g0 = __uint_as_float(g[2 * c]), g1 = __uint_as_float(g[2 * c + 1]);
                             const float u0 = __uint_as_float(u[2 * c]), u1 = __uint_as_float(u[2 * c + 1]);
-                            // silu(g) = g / (1 + exp(-g)), tests/moe_cpu_sim.cpp:155-158
+                            // silu(g) = g / (1 + exp(-g)), tests/moe_cpu_sim.cpp:155-158.  The
+                            // fast exp / divide intrinsics err by ~1e-6 relative, far below
+                            // the fp16 rounding (~5e-4) that h gets next.
+#if MOE_GEMM_ACCURATE_SILU
                             const float h0 = g0 / (1.0f + expf(-g0)) * u0;
                             const float h1 = g1 / (1.0f + expf(-g1)) * u1;
+#else
+                            const float h0 = __fdividef(g0 * u0, 1.0f + __expf(-g0));
+                            const float h1 = __fdividef(g1 * u1, 1.0f + __expf(-g1));
+#endif
                             pk[c] = pack_half2(h0, h1);
                         }
                         const int cb = col0 + j * 32;
-#pragma unroll
-                        for (int v = 0; v < 4; v++)
-                            if (cb + v * 8 + 8 <= args.nvalid)
-                                *reinterpret_cast<uint4*>(dst + j * 32 + v * 8) =
-                                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                        const int nb = min(32, args.nvalid - cb) * 2;
+                        const uint4 vv[4] = {make_uint4(pk[0], pk[1], pk[2], pk[3]), make_uint4(pk[4], pk[5], pk[6], pk[7]),
+                                             make_uint4(pk[8], pk[9], pk[10], pk[11]),
+                                             make_uint4(pk[12], pk[13], pk[14], pk[15])};
+                        if (nb > 0 && !MOE_GEMM_NOSTORE)
+                            epi_warp_store(stg_warp, lane, vv, valid ? dst + j * 32 : nullptr, nb);
                     }
                 }
             } else {
@@ -303,7 +370,19 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     uint32_t v32[32];
                     tmem_ld_32x32b_x32(tbase + j * 32, v32);
                     tmem_ld_wait();
-                    if (valid) {
+                    if (!MOE_GEMM_NOSTORE && MODE == MODE_DOWN) {  // warp-collective
+                        const int cb = col0 + j * 32;
+                        const int nb = min(32, args.nvalid - cb) * 2;
+                        uint4 vv[4];
+#pragma unroll
+                        for (int v = 0; v < 4; v++) {
+                            vv[v].x = pack_half2(__uint_as_float(v32[8 * v + 0]), __uint_as_float(v32[8 * v + 1]));
+                            vv[v].y = pack_half2(__uint_as_float(v32[8 * v + 2]), __uint_as_float(v32[8 * v + 3]));
+                            vv[v].z = pack_half2(__uint_as_float(v32[8 * v + 4]), __uint_as_float(v32[8 * v + 5]));
+                            vv[v].w = pack_half2(__uint_as_float(v32[8 * v + 6]), __uint_as_float(v32[8 * v + 7]));
+                        }
+                        if (nb > 0) epi_warp_store(stg_warp, lane, vv, valid ? dst + j * 32 : nullptr, nb);
+                    } else if (valid && !MOE_GEMM_NOSTORE) {  // peer destinations: plain stores
                         const int cb = col0 + j * 32;
 #pragma unroll
                         for (int v = 0; v < 4; v++) {
