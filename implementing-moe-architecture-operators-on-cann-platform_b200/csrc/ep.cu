@@ -370,10 +370,9 @@ ep_p2p_combine_kernel(const __half* __restrict__ ret, const int32_t* __restrict_
                       const __half* __restrict__ weights, __half* __restrict__ y, int T, int H, int K,
                       const unsigned long long* flag, unsigned long long target, int* err)
 {
-    __shared__ int ok;
-    if (threadIdx.x == 0) ok = ep_wait_flag(flag, target, err, EP_ERR_WAIT_RET);
+    // on timeout the rows are stale; the error word says so
+    if (threadIdx.x == 0) ep_wait_flag(flag, target, err, EP_ERR_WAIT_RET);
     __syncthreads();
-    (void)ok;  // on timeout the rows are stale; the error word says so
     const int vpr = H >> 3;
     const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (v >= (long long)T * vpr) return;

@@ -1,201 +1,371 @@
-// routing.cu -- MoeRoutingTopK on sm_100a: gating GEMV, softmax, top-K, renormalise.
+// routing.cu -- MoeRoutingTopK on sm_100a: gating GEMM on the tensor cores, then
+// softmax, top-K and renormalisation per token.
 //
 // Replaces op_kernel/moe_routing.cpp (Ascend Cube GEMM + scalar softmax/top-2).
 // Semantics follow the fp32 naive reference, tests/moe_cpu_sim.cpp:198-243:
-//   logits[t,e] = sum_h x[t,h] * w_gate[h,e]   (fp32, h ascending)
-//   probs       = exp(logits - max) / sum      (sum in e ascending order)
+//   logits[t,e] = sum_h x[t,h] * w_gate[h,e]      (fp32 accumulation)
+//   probs       = exp(logits - max) / sum         (sum in e ascending order)
 //   ids         = top-K of probs, descending, equal probs -> lower expert id
 //   weights     = probs[ids] / sum_k probs[ids]   -> fp16 (round to nearest even)
 //
-// Why the gating dot product keeps the reference's sequential order: x and w_gate
-// are fp16, so each product x*w is exact in fp32 and fmaf(x, w, acc) rounds exactly
-// like the reference's `dot += x*w`.  Accumulating h in ascending order per
-// (token, expert) therefore reproduces the reference logits bit for bit, and the
-// expert ids can only differ from the reference through expf() rounding at
-// (near-)ties.  The cost is a dependent FMA chain of length H per (t,e), which
-// still finishes in a few microseconds because a block runs 256 such chains and
-// 4 tokens/thread at large E give independent chains for ILP.
+// The gating product is a skinny GEMM [T,H] x [H,E]; it is HBM-bound (x is read
+// once), so it runs as tcgen05.mma with M=128 tokens per CTA, N=E rounded up to a
+// multiple of 16, K=16 per instruction and the fp32 accumulator in TMEM.  The
+// products of fp16 values are exact; the tensor core's fp32 accumulation order
+// differs from the reference's sequential sum, so logits can differ in the last
+// bits, and expert ids can only differ at (near-)ties -- the parity tests
+// compare ids bit for bit away from ties (top-K logit margin >= 1e-3).
 //
-// Data layout: a block owns TT tokens.  The H axis is walked in chunks of HC
-// elements; each chunk of x ([TT][HC]) and of w_gate (transposed to [E][HC+8],
-// padded so the 16-byte reads of different experts fall in different banks) is
-// staged in shared memory with 16-byte global loads; x is read from HBM once.
+// Per CTA: x tiles [128 tokens x 64 h] arrive by TMA (128-byte swizzle, K-major);
+// w_gate [H,E] is tiny and L2-resident, so the threads copy its [64 h x E] block
+// transposed into the K-major, 128-byte-swizzled B tile; a 4-stage ring keeps
+// three k-blocks in flight, and the w_gate loads for a refill are issued a step early.  Afterwards each thread owns one token (one TMEM lane): the E
+// logits go through shared memory and the thread runs softmax and top-K in the
+// reference's order.
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
 namespace moe {
 
-constexpr int RT_THREADS = 256;
-constexpr int RT_MAXP = 16;  // token chains per thread (E up to 256)
+constexpr int RT_BM = 128;     // tokens per CTA (UMMA M)
+constexpr int RT_BK = 64;      // h per stage (one 128-byte swizzle row)
+constexpr int RT_MAX_STAGES = 8;  // ring depth: as many as fit (>= 2)
+constexpr int RT_THREADS = 128;
+constexpr int RT_A_BYTES = RT_BM * RT_BK * 2;  // 16 KB
 
-struct RoutingPlan {
-    int tpe;  // tokens processed in parallel per pass (256 / E)
-    int P;    // chains per thread
-    int TT;   // tokens per block = tpe * P
-    int HC;   // H chunk (multiple of 8)
-    size_t smem;
+struct RoutingSmemTail {
+    uint64_t full[RT_MAX_STAGES];   // A tile landed (TMA)
+    uint64_t mdone[RT_MAX_STAGES];  // MMAs that read this stage are done
+    uint32_t tmem_base;
+    int abort_flag;
 };
 
-static RoutingPlan routing_plan(int H, int E)
+static inline int routing_epad(int E) { return (E + 15) & ~15; }
+
+// Bytes before the barrier tail: the A ring plus either per-stage B tiles or (RESIDENT)
+// all of w_gate^T as one B tile per k-block; the logits later reuse the front.
+__host__ __device__ inline size_t routing_region_bytes(bool resident, int E, int epad, int nk, int nst)
 {
-    RoutingPlan p;
-    p.tpe = RT_THREADS / E;
-    int want = (16 + p.tpe - 1) / p.tpe;  // >= 16 tokens per block
-    p.P = 1;
-    while (p.P < want && p.P < RT_MAXP) p.P *= 2;
-    p.TT = p.tpe * p.P;
-    int hc = 16384 / E;
-    if (16384 / p.TT < hc) hc = 16384 / p.TT;
-    if (hc > 512) hc = 512;
-    hc &= ~7;
-    if (hc < 8) hc = 8;
-    if (hc > H) hc = (H + 7) & ~7;
-    p.HC = hc;
-    // xs [TT][HC] fp16, ws [E][HC+8] fp16, logits [TT][E] fp32
-    p.smem = (size_t)p.TT * p.HC * 2 + (size_t)E * (p.HC + 8) * 2 + (size_t)p.TT * E * 4;
-    return p;
+    const size_t ring = resident ? (size_t)nst * RT_A_BYTES + (size_t)nk * epad * 128
+                                 : (size_t)nst * (RT_A_BYTES + (size_t)epad * 128);
+    const size_t logits = (size_t)RT_BM * (E + 1) * 4;
+    return ((ring > logits ? ring : logits) + 15) & ~(size_t)15;
 }
 
-// P (token chains per thread) is a template parameter so that the accumulators
-// are indexed statically and stay in registers.
-template <int P>
-__global__ void __launch_bounds__(RT_THREADS)
-routing_topk_kernel(const __half* __restrict__ x, const __half* __restrict__ w_gate,
-                    int32_t* __restrict__ expert_ids, __half* __restrict__ weights, int T, int H,
-                    int E, int K, int tpe, int TT, int HC)
+static size_t routing_smem_bytes(bool resident, int E, int epad, int nk, int nst)
 {
-    extern __shared__ __align__(16) uint8_t rt_smem[];
-    __half* xs = reinterpret_cast<__half*>(rt_smem);                  // [TT][HC]
-    __half* ws = xs + (size_t)TT * HC;                                 // [E][HC+8]
-    float* lg = reinterpret_cast<float*>(ws + (size_t)E * (HC + 8));   // [TT][E]
-    const int wstride = HC + 8;
+    return 1024 + routing_region_bytes(resident, E, epad, nk, nst) + sizeof(RoutingSmemTail) + 64;
+}
 
-    const int tid = threadIdx.x;
-    const int t_base = blockIdx.x * TT;
-    const bool active = tid < tpe * E;
-    const int e = tid % E;
-    const int tslot = tid / E;
+// Byte offset of element (row n, k) of a K-major tile with 128-byte rows and the
+// 128-byte swizzle: 8-row atoms of 1024 bytes, 16-byte chunk index XOR (row % 8).
+__device__ __forceinline__ uint32_t sw128_offset(int n, int k)
+{
+    return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((k >> 3) ^ (n & 7)) & 7) << 4) + (k & 7) * 2);
+}
 
-    float acc[P];
-#pragma unroll
-    for (int j = 0; j < P; j++) acc[j] = 0.0f;
+__device__ int g_routing_err;
 
-    for (int h0 = 0; h0 < H; h0 += HC) {
-        const int hc = min(HC, H - h0);  // multiple of 8 because H is
-        const int vec_per_row = hc >> 3;
-        // stage x chunk: TT rows x hc halves, 16-byte loads
-        for (int v = tid; v < TT * vec_per_row; v += RT_THREADS) {
-            int r = v / vec_per_row, c = (v - r * vec_per_row) << 3;
-            int t = t_base + r;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (t < T) val = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + h0 + c));
-            *reinterpret_cast<uint4*>(xs + (size_t)r * HC + c) = val;
+template <bool RESIDENT>
+__global__ void __launch_bounds__(RT_THREADS)
+routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restrict__ w_gate,
+                  int32_t* __restrict__ expert_ids, __half* __restrict__ weights, int T, int H, int E, int K,
+                  int epad, uint32_t tmem_cols, int nst, int* err)
+{
+    extern __shared__ uint8_t rt_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(rt_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const size_t stage_bytes = (size_t)RT_A_BYTES + (size_t)epad * 128;  // non-resident stages
+    const int nk = (H + RT_BK - 1) / RT_BK;
+    RoutingSmemTail* tail =
+        reinterpret_cast<RoutingSmemTail*>(smem + routing_region_bytes(RESIDENT, E, epad, nk, nst));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int t0 = blockIdx.x * RT_BM;
+    volatile int* abort_flag = &tail->abort_flag;
+    // MoeRoutingTopK has no workspace: a timed-out wait is recorded in a device
+    // global (the waits still end the kernel instead of spinning forever)
+    int* errp = err ? err : &g_routing_err;
+
+    if (tid == 0) {
+        for (int s = 0; s < nst; s++) {
+            mbar_init(smem_u32(&tail->full[s]), 1);
+            mbar_init(smem_u32(&tail->mdone[s]), 1);
         }
-        // stage w_gate chunk transposed: ws[e][h] = w_gate[h0+h][e]; h-fastest so the
-        // shared-memory stores of a warp are consecutive (w_gate itself is L2-resident)
-        for (int v = tid; v < hc * E; v += RT_THREADS) {
-            int ee = v / hc, h = v - ee * hc;
-            ws[(size_t)ee * wstride + h] = __ldg(w_gate + (size_t)(h0 + h) * E + ee);
+        tail->abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmX);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&tail->tmem_base), tmem_cols);
+        tmem_relinquish();
+    }
+    // B rows >= E stay zero for the whole kernel
+    {
+        const int ntiles = RESIDENT ? nk : nst;
+        for (int tt = 0; tt < ntiles; tt++) {
+            uint8_t* bt = RESIDENT ? smem + nst * (size_t)RT_A_BYTES + (size_t)tt * epad * 128
+                                   : smem + tt * stage_bytes + RT_A_BYTES;
+            for (int i = tid; i < (epad - E) * 8; i += RT_THREADS) {
+                const int n = E + i / 8, c = i % 8;
+                *reinterpret_cast<uint4*>(bt + sw128_offset(n, c * 8)) = make_uint4(0, 0, 0, 0);
+            }
         }
-        __syncthreads();
-        if (active) {
-            const __half* wrow = ws + (size_t)e * wstride;
-            for (int h = 0; h < hc; h += 8) {
-                uint4 wv = *reinterpret_cast<const uint4*>(wrow + h);
-                const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
-                float wf[8];
+    }
+
+    uint8_t* bres = smem + nst * (size_t)RT_A_BYTES;  // RESIDENT: all of w_gate^T, one tile per k-block
+    auto b_tile = [&](int kb, int s) -> uint8_t* {
+        return RESIDENT ? bres + (size_t)kb * epad * 128 : smem + s * stage_bytes + RT_A_BYTES;
+    };
+    // w_gate rows [h_begin, h_end) -> swizzled K-major B tiles.  The rows are one
+    // contiguous block of (h_end-h_begin)*E halves: read it with 16-byte loads, 8 in
+    // flight per thread, and scatter each half to (row n = expert, k = h % 64) of the
+    // tile of k-block h / 64 (tile_of(kb) gives its address).
+    auto b_fill_rows = [&](int h_begin, int h_end, auto tile_of) {
+        const uint4* src = reinterpret_cast<const uint4*>(w_gate + (size_t)h_begin * E);
+        const int nvec = ((h_end - h_begin) * E) >> 3;  // H*E and 64*E are multiples of 8
+        for (int v0 = tid; v0 < nvec; v0 += 8 * RT_THREADS) {
+            uint4 buf[8];
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    float2 f = __half22float2(w2[q]);
-                    wf[2 * q] = f.x;
-                    wf[2 * q + 1] = f.y;
-                }
+            for (int u = 0; u < 8; u++) {
+                const int v = v0 + u * RT_THREADS;
+                buf[u] = v < nvec ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
-                for (int j = 0; j < P; j++) {
-                    {
-                        const int r = tslot + j * tpe;
-                        uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)r * HC + h);
-                        const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
-                        float a = acc[j];
+            for (int u = 0; u < 8; u++) {
+                const int v = v0 + u * RT_THREADS;
+                if (v >= nvec) break;
+                const unsigned short* hv = reinterpret_cast<const unsigned short*>(&buf[u]);
+                int f = 8 * v;
+                int hh = h_begin + f / E, n = f - (f / E) * E;
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            float2 f = __half22float2(x2[q]);
-                            a = fmaf(f.x, wf[2 * q], a);      // exact product, one rounding
-                            a = fmaf(f.y, wf[2 * q + 1], a);  // == reference `dot += x*w`
-                        }
-                        acc[j] = a;
-                    }
+                for (int j = 0; j < 8; j++) {
+                    *reinterpret_cast<unsigned short*>(tile_of(hh / RT_BK) + sw128_offset(n, hh % RT_BK)) = hv[j];
+                    if (++n == E) { n = 0; ++hh; }
                 }
             }
         }
+    };
+    // one k-block (non-resident stages): rows beyond H are zero
+    auto b_fill = [&](int kb, uint8_t* bt) {
+        const int h0 = kb * RT_BK, h1 = min(H, h0 + RT_BK);
+        if (h1 - h0 < RT_BK)
+            for (int i = tid; i < epad * 8; i += RT_THREADS)
+                *reinterpret_cast<uint4*>(bt + sw128_offset(i / 8, (i % 8) * 8)) = make_uint4(0, 0, 0, 0);
+        if (h1 - h0 < RT_BK) __syncthreads();
+        b_fill_rows(h0, h1, [&](int) { return bt; });
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B is read by the tensor core
+    };
+    auto a_load = [&](int kb, int s) {  // thread 0
+        const uint32_t full = smem_u32(&tail->full[s]);
+        mbar_arrive_expect_tx(full, RT_A_BYTES);
+        tma_load_2d(smem_u32(smem + s * (RESIDENT ? (size_t)RT_A_BYTES : stage_bytes)), &tmX, full, kb * RT_BK, t0,
+                    l2_policy_evict_first());
+    };
+    auto a_addr = [&](int s) -> uint32_t {
+        return smem_u32(smem + s * (RESIDENT ? (size_t)RT_A_BYTES : stage_bytes));
+    };
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tail->tmem_base;
+    const uint32_t idesc = umma_idesc_f16_f32(RT_BM, epad);
+    bool ok = true;
+
+    if (RESIDENT) {
+        // A ring by TMA starts at once; meanwhile every thread transposes w_gate in
+        if (tid == 0)
+            for (int kb = 0; kb < nk && kb < nst; kb++) a_load(kb, kb);
+        if (H % RT_BK) {  // the last tile's rows beyond H are zero
+            uint8_t* bt = b_tile(nk - 1, 0);
+            for (int i = tid; i < epad * 8; i += RT_THREADS)
+                *reinterpret_cast<uint4*>(bt + sw128_offset(i / 8, (i % 8) * 8)) = make_uint4(0, 0, 0, 0);
+            __syncthreads();
+        }
+        b_fill_rows(0, H, [&](int kb) { return b_tile(kb, 0); });
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
-    }
-    if (active) {
+        if (tid == 0) {
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % nst;
+                if (!mbar_wait_bounded(smem_u32(&tail->full[s]), (kb / nst) & 1u, errp, MOE_DEV_WAIT_TIMEOUT_MMA,
+                                       abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = a_addr(s), b = smem_u32(b_tile(kb, s));
 #pragma unroll
-        for (int j = 0; j < P; j++) lg[(size_t)(tslot + j * tpe) * E + e] = acc[j];
+                for (int k = 0; k < RT_BK / 16; k++)
+                    umma_f16_ss(tmem_base, umma_desc_sw128(a + k * 32), umma_desc_sw128(b + k * 32), idesc,
+                                (kb | k) != 0);
+                umma_commit(smem_u32(&tail->mdone[s]));
+                // refill the stage MMA kb-1 read, once that MMA is done
+                const int nb = kb - 1 + nst;
+                if (kb >= 1 && nb < nk) {
+                    const int sn = nb % nst;
+                    if (!mbar_wait_bounded(smem_u32(&tail->mdone[sn]), ((kb - 1) / nst) & 1u, errp,
+                                           MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    a_load(nb, sn);
+                }
+            }
+        }
+    } else {
+        const int pro = nk < nst ? nk : nst;
+        for (int kb = 0; kb < pro; kb++) {
+            if (tid == 0) a_load(kb, kb);
+            b_fill(kb, b_tile(kb, kb));
+        }
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % nst;
+            const uint32_t par = (kb / nst) & 1u;
+            __syncthreads();  // every thread's B stores for this stage are in
+            if (tid == 0) {
+                if (ok && mbar_wait_bounded(smem_u32(&tail->full[s]), par, errp, MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                    tc_fence_after();
+                    const uint32_t a = a_addr(s), b = smem_u32(b_tile(kb, s));
+#pragma unroll
+                    for (int k = 0; k < RT_BK / 16; k++)
+                        umma_f16_ss(tmem_base, umma_desc_sw128(a + k * 32), umma_desc_sw128(b + k * 32), idesc,
+                                    (kb | k) != 0);
+                } else {
+                    ok = false;
+                }
+                umma_commit(smem_u32(&tail->mdone[s]));
+            }
+            if (kb + nst < nk) {  // refill stage s once the MMAs that read it are done
+                if (!mbar_wait_bounded(smem_u32(&tail->mdone[s]), par, errp, MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag))
+                    ok = false;
+                if (tid == 0) a_load(kb + nst, s);
+                b_fill(kb + nst, b_tile(kb + nst, s));
+            }
+        }
     }
     __syncthreads();
-
-    // softmax + top-K: one thread per token, reference order (moe_cpu_sim.cpp:211-243)
-    if (tid < TT) {
-        const int t = t_base + tid;
-        if (t < T) {
-            float* l = lg + (size_t)tid * E;
-            float maxv = -1e30f;
-            for (int i = 0; i < E; i++) maxv = l[i] > maxv ? l[i] : maxv;
-            float sum = 0.0f;
-            for (int i = 0; i < E; i++) {
-                float pe = expf(l[i] - maxv);
-                l[i] = pe;  // l now holds unnormalised probs
-                sum += pe;
-            }
-            for (int i = 0; i < E; i++) l[i] = l[i] / sum;
-            // top-K selection: K passes, strict '>' keeps the lower id on ties.
-            // Selected entries are marked by negating (probs are >= 0; -1 - p < 0).
-            int sel[8];
-            float ps[8];
-            float wsum = 0.0f;
-            for (int k = 0; k < K; k++) {
-                int best = -1;
-                float bv = 0.0f;
-                for (int i = 0; i < E; i++) {
-                    float v = l[i];
-                    if (v < 0.0f) continue;
-                    if (best < 0 || v > bv) { best = i; bv = v; }
-                }
-                sel[k] = best;
-                ps[k] = bv;
-                l[best] = -1.0f - bv;
-                wsum += bv;
-            }
-            for (int k = 0; k < K; k++) {
-                expert_ids[(size_t)t * K + k] = sel[k];
-                weights[(size_t)t * K + k] = __float2half_rn(ps[k] / wsum);
-            }
+    if (!ok && tid == 0) {
+        // unwinding after a timeout: wait (bounded) for TMA copies still in flight
+        for (int kb = nk > nst ? nk - nst : 0; kb < nk; kb++) {
+            const uint64_t w0 = global_timer_ns();
+            while (!mbar_try_wait(smem_u32(&tail->full[kb % nst]), (kb / nst) & 1u))
+                if (global_timer_ns() - w0 > MOE_WAIT_LIMIT_NS) break;
         }
+    }
+    // the last commit covers every MMA of this CTA
+    {
+        const int s = (nk - 1) % nst;
+        mbar_wait_bounded(smem_u32(&tail->mdone[s]), ((nk - 1) / nst) & 1u, errp, MOE_DEV_WAIT_TIMEOUT_EPI,
+                          abort_flag);
+    }
+    tc_fence_after();
+    __syncthreads();
+
+    // logits: TMEM lane r (this thread's token) -> shared [128][E+1]
+    float* lg = reinterpret_cast<float*>(smem);
+    const int r = tid;  // warp w reads TMEM lanes 32w..32w+31
+    const uint32_t tbase = tmem_base + ((uint32_t)(warp * 32) << 16);
+    for (int c0 = 0; c0 < epad; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            if (c0 + j < E) lg[(size_t)r * (E + 1) + c0 + j] = __uint_as_float(v[j]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, tmem_cols);
+    }
+
+    // softmax + top-K for this thread's token, reference order (moe_cpu_sim.cpp:211-243)
+    const int t = t0 + r;
+    if (t < T) {
+        float* l = lg + (size_t)r * (E + 1);
+        float maxv = -1e30f;
+        for (int i = 0; i < E; i++) maxv = l[i] > maxv ? l[i] : maxv;
+        float sum = 0.0f;
+        for (int i = 0; i < E; i++) {
+            const float pe = expf(l[i] - maxv);
+            l[i] = pe;
+            sum += pe;
+        }
+        for (int i = 0; i < E; i++) l[i] = l[i] / sum;
+        float wsum = 0.0f;
+        float selp[8];
+        for (int k = 0; k < K; k++) {  // K passes; strict '>' keeps the lower id on ties
+            int best = -1;
+            float bv = 0.0f;
+            for (int i = 0; i < E; i++) {
+                const float v = l[i];
+                if (v < 0.0f) continue;
+                if (best < 0 || v > bv) { best = i; bv = v; }
+            }
+            expert_ids[(size_t)t * K + k] = best;
+            l[best] = -1.0f;  // selected: excluded from the next passes
+            selp[k] = bv;
+            wsum += bv;  // selection order, as the reference's wSum (moe_cpu_sim.cpp:236-240)
+        }
+        for (int k = 0; k < K; k++) weights[(size_t)t * K + k] = __float2half_rn(selp[k] / wsum);
     }
 }
 
-cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights,
-                           int T, int H, int E, int K, cudaStream_t s)
+typedef CUresult (*RtEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights, int T, int H,
+                           int E, int K, cudaStream_t s)
 {
     if (T == 0) return cudaSuccess;
-    RoutingPlan p = routing_plan(H, E);
-    const int grid = (T + p.TT - 1) / p.TT;
-    switch (p.P) {
-#define MOE_ROUTING_CASE(PP)                                                                       \
-    case PP:                                                                                       \
-        routing_topk_kernel<PP><<<grid, RT_THREADS, p.smem, s>>>(x, w_gate, ids, weights, T, H, E, \
-                                                                 K, p.tpe, p.TT, p.HC);             \
-        break;
-        MOE_ROUTING_CASE(1)
-        MOE_ROUTING_CASE(2)
-        MOE_ROUTING_CASE(4)
-        MOE_ROUTING_CASE(8)
-        MOE_ROUTING_CASE(16)
-#undef MOE_ROUTING_CASE
-        default: return cudaErrorInvalidValue;
+    static RtEncodeTiledFn enc = nullptr;
+    if (!enc) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return cudaErrorInvalidValue;
+        enc = reinterpret_cast<RtEncodeTiledFn>(p);
     }
+    CUtensorMap tm;
+    cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+    cuuint32_t box[2] = {RT_BK, RT_BM};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    const int epad = routing_epad(E);
+    const int nk = (H + RT_BK - 1) / RT_BK;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)epad) cols <<= 1;
+    // all of w_gate^T resident in shared memory when it fits (the benchmark's E=16:
+    // 64 KB at H=2048), else per-stage B tiles
+    const size_t cap = 210 * 1024;
+    const bool resident = routing_smem_bytes(true, E, epad, nk, 4) <= cap;
+    int nst = RT_MAX_STAGES;
+    while (nst > 2 && routing_smem_bytes(resident, E, epad, nk, nst) > cap) nst--;
+    const size_t smem = routing_smem_bytes(resident, E, epad, nk, nst);
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(routing_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(routing_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    }
+    const int grid = (T + RT_BM - 1) / RT_BM;
+    if (resident)
+        routing_tc_kernel<true><<<grid, RT_THREADS, smem, s>>>(tm, w_gate, ids, weights, T, H, E, K, epad, cols, nst, nullptr);
+    else
+        routing_tc_kernel<false><<<grid, RT_THREADS, smem, s>>>(tm, w_gate, ids, weights, T, H, E, K, epad, cols, nst, nullptr);
     return cudaGetLastError();
 }
 
