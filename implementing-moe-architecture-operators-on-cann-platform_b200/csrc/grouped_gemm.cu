@@ -370,7 +370,7 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     uint32_t v32[32];
                     tmem_ld_32x32b_x32(tbase + j * 32, v32);
                     tmem_ld_wait();
-                    if (!MOE_GEMM_NOSTORE && MODE == MODE_DOWN) {  // warp-collective
+                    if (!MOE_GEMM_NOSTORE) {  // warp-collective: local rows or peer rows alike
                         const int cb = col0 + j * 32;
                         const int nb = min(32, args.nvalid - cb) * 2;
                         uint4 vv[4];
@@ -382,19 +382,6 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             vv[v].w = pack_half2(__uint_as_float(v32[8 * v + 6]), __uint_as_float(v32[8 * v + 7]));
                         }
                         if (nb > 0) epi_warp_store(stg_warp, lane, vv, valid ? dst + j * 32 : nullptr, nb);
-                    } else if (valid && !MOE_GEMM_NOSTORE) {  // peer destinations: plain stores
-                        const int cb = col0 + j * 32;
-#pragma unroll
-                        for (int v = 0; v < 4; v++) {
-                            if (cb + v * 8 + 8 <= args.nvalid) {
-                                uint4 o;
-                                o.x = pack_half2(__uint_as_float(v32[8 * v + 0]), __uint_as_float(v32[8 * v + 1]));
-                                o.y = pack_half2(__uint_as_float(v32[8 * v + 2]), __uint_as_float(v32[8 * v + 3]));
-                                o.z = pack_half2(__uint_as_float(v32[8 * v + 4]), __uint_as_float(v32[8 * v + 5]));
-                                o.w = pack_half2(__uint_as_float(v32[8 * v + 6]), __uint_as_float(v32[8 * v + 7]));
-                                *reinterpret_cast<uint4*>(dst + j * 32 + v * 8) = o;
-                            }
-                        }
                     }
                 }
             }
