@@ -137,7 +137,7 @@ def reference_inputs(cfg, moe):
     import numpy as np
 
     T, H, E, K, I, seed = moe.CONFIGS[cfg]
-    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device="cpu")
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device="cpu", zipf=moe.inputs.ZIPF.get(cfg))
     return (x.float().numpy(), wg.float().numpy(), ew.float().numpy().astype(np.float32, copy=False)), \
         (T, H, E, K, I)
 
@@ -224,7 +224,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     # every rank routes its own batch of T tokens (per-GPU work fixed as N grows);
     # the weights are one model (same seed on every rank)
-    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev)
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev, zipf=moe.inputs.ZIPF.get(args.config))
     if rank > 0:
         x = moe.make_inputs_torch(T, H, 1, 1, 8, seed + rank, device=dev)[0]
     y = torch.empty((T, H), dtype=torch.float16, device=dev)
@@ -356,13 +356,17 @@ def run_ours(args):
         hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         comb_bytes = T * K * H * 2 + T * K * 2 + T * H * 2
         rout_bytes = T * H * 2 + H * E * 2 + T * K * 6
+        ids_chk, _ = moe.moe_routing_topk(x, wg, K)
+        load = torch.bincount(ids_chk.flatten().long(), minlength=E).float() / ids_chk.numel()
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I} per GPU",
                        "global_batch": world * T, "parallelism": f"ep{world} (expert parallel, NCCL send/recv)" if world > 1 else "single GPU",
-                       "l2": "flushed between timed steps (512 MB write)", "inputs": "seeded N(0,1)/N(0,1/fan_in) fp16"},
+                       "l2": "flushed between timed steps (512 MB write)", "inputs": "seeded N(0,1)/N(0,1/fan_in) fp16" + (
+                           ", w_gate columns scaled toward Zipf s=1 expert load" if args.config in moe.inputs.ZIPF else ""),
+                       "expert_load_rank0": [round(v, 4) for v in load.tolist()]},
             "roofline": {"kernel": "gemm_swiglu (gate/up grouped GEMM + SwiGLU epilogue)", "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                          "peak_source": f"{peak_src} bf16_tflops (burst cuBLAS)",

@@ -10,7 +10,8 @@ from __future__ import annotations
 
 import numpy as np
 
-# name -> (T, H, E, K, I, seed)
+# name -> (T, H, E, K, I, seed); the Mixtral-shaped layer's router is skewed so that
+# the expert loads follow Zipf s=1 (ZIPF below)
 CONFIGS = {
     "small": (8, 64, 4, 2, 256, 42),
     "decode": (128, 2048, 16, 2, 8192, 44),
@@ -18,6 +19,30 @@ CONFIGS = {
     "mixtral": (8192, 4096, 8, 2, 14336, 44),
     "deepseek": (16384, 2048, 64, 6, 1408, 44),
 }
+ZIPF = {"mixtral": 1.0}
+
+
+def zipf_gate(x, w_gate, K, s=1.0, iters=60):
+    """Scales the columns of w_gate so the realised top-K load over the tokens x
+    follows Zipf(s) over the experts (expert e gets a share ~ 1/(e+1)^s of the
+    T*K slots).  The operator API has no router bias, so the skew lives in
+    w_gate.  Deterministic: plain fp32 torch on the tensors' device.
+    Returns (fp16 w_gate, realised per-expert load fractions)."""
+    import torch
+
+    E = w_gate.shape[1]
+    target = torch.tensor([1.0 / (e + 1) ** s for e in range(E)], device=x.device)
+    target = target / target.sum()
+    base = x.float() @ w_gate.float()  # [T, E]
+    theta = torch.zeros(E, device=x.device)
+    for _ in range(iters):
+        ids = torch.topk(base * theta.exp(), K, dim=1).indices
+        load = torch.bincount(ids.flatten(), minlength=E).float() / ids.numel()
+        theta = theta + 0.5 * (target.log() - load.clamp_min(1e-5).log())
+    wg = (w_gate.float() * theta.exp()).half()
+    ids = torch.topk(x.float() @ wg.float(), K, dim=1).indices
+    load = torch.bincount(ids.flatten(), minlength=E).float() / ids.numel()
+    return wg, load.cpu().tolist()
 
 
 def make_inputs(T, H, E, K, I, seed):
@@ -32,7 +57,7 @@ def make_inputs(T, H, E, K, I, seed):
     return x, wg, ew
 
 
-def make_inputs_torch(T, H, E, K, I, seed, device="cuda"):
+def make_inputs_torch(T, H, E, K, I, seed, device="cuda", zipf=None):
     """Same distributions drawn with torch's generator on `device` (fast at full size).
 
     The stream differs from make_inputs; every check copies the very tensors it
@@ -48,4 +73,6 @@ def make_inputs_torch(T, H, E, K, I, seed, device="cuda"):
     for e in range(E):
         ew[e, : 2 * I] = (torch.randn((2 * I, H), generator=g, device=device) / H ** 0.5).half()
         ew[e, 2 * I:] = (torch.randn((H, I), generator=g, device=device) / I ** 0.5).half().reshape(I, H)
+    if zipf:
+        wg, _ = zipf_gate(x, wg, K, zipf)
     return x, wg, ew

@@ -128,12 +128,13 @@ def test_decode_config_full(moe, O):
     check_close(y.float().cpu().numpy()[ok], O.combine(ffn, rw)[ok], "y")
 
 
-@pytest.mark.parametrize("cfg", ["prefill", "deepseek"])
+@pytest.mark.parametrize("cfg", ["prefill", "deepseek", "mixtral"])
 def test_full_size_properties(cfg, moe, O):
     """Full benchmark sizes: ids on every token, permutation bit-exact, and y on a
-    token slice against the oracle (rows are independent)."""
+    token slice against the oracle (rows are independent).  The Mixtral-shaped
+    layer runs with its Zipf-skewed router (uneven expert groups)."""
     T, H, E, K, I, seed = moe.CONFIGS[cfg]
-    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed)
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, zipf=moe.inputs.ZIPF.get(cfg))
     ws = torch.empty((moe.moe_layer_workspace_size(T, H, E, K, I),), dtype=torch.uint8, device="cuda")
     ids_d = torch.empty((T, K), dtype=torch.int32, device="cuda")
     w_d = torch.empty((T, K), dtype=torch.float16, device="cuda")
