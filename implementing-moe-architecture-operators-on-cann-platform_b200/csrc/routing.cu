@@ -22,8 +22,12 @@
 // three k-blocks in flight, and the w_gate loads for a refill are issued a step early.  Afterwards each thread owns one token (one TMEM lane): the E
 // logits go through shared memory and the thread runs softmax and top-K in the
 // reference's order.
+#include <cooperative_groups.h>
+
 #include "moe_common.cuh"
 #include "moe_kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace moe {
 
@@ -42,19 +46,23 @@ struct RoutingSmemTail {
 
 static inline int routing_epad(int E) { return (E + 15) & ~15; }
 
+// Row pitch (floats) of the logits rows in shared memory: E+4 keeps rows 16-byte
+// aligned for vector stores when E % 4 == 0, else E+1 (odd: conflict-free scalars).
+__host__ __device__ inline int routing_pitch(int E) { return (E % 4 == 0) ? E + 4 : E + 1; }
+
 // Bytes before the barrier tail: the A ring plus either per-stage B tiles or (RESIDENT)
 // all of w_gate^T as one B tile per k-block; the logits later reuse the front.
-__host__ __device__ inline size_t routing_region_bytes(bool resident, int E, int epad, int nk, int nst)
+__host__ __device__ inline size_t routing_region_bytes(bool resident, int E, int epad, int nk, int nst, int S)
 {
     const size_t ring = resident ? (size_t)nst * RT_A_BYTES + (size_t)nk * epad * 128
                                  : (size_t)nst * (RT_A_BYTES + (size_t)epad * 128);
-    const size_t logits = (size_t)RT_BM * (E + 1) * 4;
+    const size_t logits = (size_t)S * RT_BM * routing_pitch(E) * 4;  // one slot of partial logits per cluster rank
     return ((ring > logits ? ring : logits) + 15) & ~(size_t)15;
 }
 
-static size_t routing_smem_bytes(bool resident, int E, int epad, int nk, int nst)
+static size_t routing_smem_bytes(bool resident, int E, int epad, int nk, int nst, int S)
 {
-    return 1024 + routing_region_bytes(resident, E, epad, nk, nst) + sizeof(RoutingSmemTail) + 64;
+    return 1024 + routing_region_bytes(resident, E, epad, nk, nst, S) + sizeof(RoutingSmemTail) + 64;
 }
 
 // Byte offset of element (row n, k) of a K-major tile with 128-byte rows and the
@@ -66,26 +74,42 @@ __device__ __forceinline__ uint32_t sw128_offset(int n, int k)
 
 __device__ int g_routing_err;
 
+#ifdef MOE_ROUTING_PROBE  // development builds only: phase timestamps of CTA 0
+__device__ unsigned long long g_rt_probe[8];
+#define RT_STAMP(i) \
+    if (blockIdx.x == 0 && threadIdx.x == 0) g_rt_probe[i] = global_timer_ns();
+#else
+#define RT_STAMP(i)
+#endif
+
 template <bool RESIDENT>
 __global__ void __launch_bounds__(RT_THREADS)
 routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restrict__ w_gate,
                   int32_t* __restrict__ expert_ids, __half* __restrict__ weights, int T, int H, int E, int K,
-                  int epad, uint32_t tmem_cols, int nst, int* err)
+                  int epad, uint32_t tmem_cols, int nst, int nkl_max, int* err)
 {
+    // A cluster of S CTAs shares one 128-token tile; CTA rank c handles k-blocks
+    // [c*nk/S, (c+1)*nk/S) and rank 0 sums the partial logits in rank order.
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = (int)cluster.num_blocks();
+    const int crank = (int)cluster.block_rank();
     extern __shared__ uint8_t rt_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(rt_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const size_t stage_bytes = (size_t)RT_A_BYTES + (size_t)epad * 128;  // non-resident stages
-    const int nk = (H + RT_BK - 1) / RT_BK;
+    const int nk_all = (H + RT_BK - 1) / RT_BK;
+    const int kb0 = crank * nk_all / S, kb1 = (crank + 1) * nk_all / S;
+    const int nk = kb1 - kb0;  // this CTA's k-blocks (local index kb <-> global kb0 + kb)
     RoutingSmemTail* tail =
-        reinterpret_cast<RoutingSmemTail*>(smem + routing_region_bytes(RESIDENT, E, epad, nk, nst));
+        reinterpret_cast<RoutingSmemTail*>(smem + routing_region_bytes(RESIDENT, E, epad, nkl_max, nst, S));
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int t0 = blockIdx.x * RT_BM;
+    const int t0 = (blockIdx.x / S) * RT_BM;
     volatile int* abort_flag = &tail->abort_flag;
     // MoeRoutingTopK has no workspace: a timed-out wait is recorded in a device
     // global (the waits still end the kernel instead of spinning forever)
     int* errp = err ? err : &g_routing_err;
 
+    RT_STAMP(0)
     if (tid == 0) {
         for (int s = 0; s < nst; s++) {
             mbar_init(smem_u32(&tail->full[s]), 1);
@@ -146,8 +170,8 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
         }
     };
     // one k-block (non-resident stages): rows beyond H are zero
-    auto b_fill = [&](int kb, uint8_t* bt) {
-        const int h0 = kb * RT_BK, h1 = min(H, h0 + RT_BK);
+    auto b_fill = [&](int kb, uint8_t* bt) {  // local k-block kb
+        const int h0 = (kb0 + kb) * RT_BK, h1 = min(H, h0 + RT_BK);
         if (h1 - h0 < RT_BK)
             for (int i = tid; i < epad * 8; i += RT_THREADS)
                 *reinterpret_cast<uint4*>(bt + sw128_offset(i / 8, (i % 8) * 8)) = make_uint4(0, 0, 0, 0);
@@ -158,7 +182,7 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
     auto a_load = [&](int kb, int s) {  // thread 0
         const uint32_t full = smem_u32(&tail->full[s]);
         mbar_arrive_expect_tx(full, RT_A_BYTES);
-        tma_load_2d(smem_u32(smem + s * (RESIDENT ? (size_t)RT_A_BYTES : stage_bytes)), &tmX, full, kb * RT_BK, t0,
+        tma_load_2d(smem_u32(smem + s * (RESIDENT ? (size_t)RT_A_BYTES : stage_bytes)), &tmX, full, (kb0 + kb) * RT_BK, t0,
                     l2_policy_evict_first());
     };
     auto a_addr = [&](int s) -> uint32_t {
@@ -176,15 +200,17 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
         // A ring by TMA starts at once; meanwhile every thread transposes w_gate in
         if (tid == 0)
             for (int kb = 0; kb < nk && kb < nst; kb++) a_load(kb, kb);
-        if (H % RT_BK) {  // the last tile's rows beyond H are zero
+        if ((H % RT_BK) && kb1 == nk_all) {  // the last tile's rows beyond H are zero
             uint8_t* bt = b_tile(nk - 1, 0);
             for (int i = tid; i < epad * 8; i += RT_THREADS)
                 *reinterpret_cast<uint4*>(bt + sw128_offset(i / 8, (i % 8) * 8)) = make_uint4(0, 0, 0, 0);
             __syncthreads();
         }
-        b_fill_rows(0, H, [&](int kb) { return b_tile(kb, 0); });
+        RT_STAMP(1)
+        b_fill_rows(kb0 * RT_BK, min(H, kb1 * RT_BK), [&](int kbg) { return b_tile(kbg - kb0, 0); });
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
+        RT_STAMP(2)
         if (tid == 0) {
             for (int kb = 0; kb < nk; kb++) {
                 const int s = kb % nst;
@@ -261,18 +287,32 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
     }
     tc_fence_after();
     __syncthreads();
+    RT_STAMP(3)
 
-    // logits: TMEM lane r (this thread's token) -> shared [128][E+1]
-    float* lg = reinterpret_cast<float*>(smem);
+    // logits: TMEM lane r (this thread's token) -> row r of slot `crank` of the
+    // leader's shared memory ([S][128][E+1]; with S == 1 that is this CTA's own)
     const int r = tid;  // warp w reads TMEM lanes 32w..32w+31
+    if (S > 1) cluster.sync();  // every CTA of the cluster is done with its ring (the slots overlap it)
+    float* lg = reinterpret_cast<float*>(smem);
+    const int pitch = routing_pitch(E);
+    float* dst = (S > 1 ? cluster.map_shared_rank(lg, 0) : lg) + ((size_t)crank * RT_BM + r) * pitch;
     const uint32_t tbase = tmem_base + ((uint32_t)(warp * 32) << 16);
     for (int c0 = 0; c0 < epad; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + c0, v);
         tmem_ld_wait();
+        if ((E & 3) == 0) {  // 16-byte stores (fewer distributed-shared-memory transactions)
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (c0 + j < E) lg[(size_t)r * (E + 1) + c0 + j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 32; j += 4)
+                if (c0 + j < E)
+                    *reinterpret_cast<float4*>(dst + c0 + j) =
+                        make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                    __uint_as_float(v[j + 3]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (c0 + j < E) dst[c0 + j] = __uint_as_float(v[j]);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -280,11 +320,37 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
         tc_fence_after();
         tmem_dealloc(tmem_base, tmem_cols);
     }
-
+    if (S > 1) {
+        RT_STAMP(6)
+        cluster.sync();  // all partial slots have landed in the leader
+        RT_STAMP(7)
+        if (crank != 0) return;
+        // rank 0: slot 0 += slot 1 + ... in rank order (deterministic)
+        float* mine = lg + (size_t)r * pitch;
+        if ((E & 3) == 0) {
+            for (int i = 0; i < E; i += 4) {
+                float4 a = *reinterpret_cast<const float4*>(mine + i);
+                for (int c = 1; c < S; c++) {
+                    const float4 o = *reinterpret_cast<const float4*>(lg + ((size_t)c * RT_BM + r) * pitch + i);
+                    a.x += o.x;
+                    a.y += o.y;
+                    a.z += o.z;
+                    a.w += o.w;
+                }
+                *reinterpret_cast<float4*>(mine + i) = a;
+            }
+        } else {
+            for (int c = 1; c < S; c++) {
+                const float* o = lg + ((size_t)c * RT_BM + r) * pitch;
+                for (int i = 0; i < E; i++) mine[i] += o[i];
+            }
+        }
+    }
+    RT_STAMP(4)
     // softmax + top-K for this thread's token, reference order (moe_cpu_sim.cpp:211-243)
     const int t = t0 + r;
     if (t < T) {
-        float* l = lg + (size_t)r * (E + 1);
+        float* l = lg + (size_t)r * pitch;
         float maxv = -1e30f;
         for (int i = 0; i < E; i++) maxv = l[i] > maxv ? l[i] : maxv;
         float sum = 0.0f;
@@ -311,6 +377,15 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
         }
         for (int k = 0; k < K; k++) weights[(size_t)t * K + k] = __float2half_rn(selp[k] / wsum);
     }
+    __syncthreads();
+    RT_STAMP(5)
+}
+
+static int dev_of_current()
+{
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
 }
 
 typedef CUresult (*RtEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -345,11 +420,24 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
     while (cols < (uint32_t)epad) cols <<= 1;
     // all of w_gate^T resident in shared memory when it fits (the benchmark's E=16:
     // 64 KB at H=2048), else per-stage B tiles
+    // cluster split along H: enough CTAs to cover the SMs when there are few tiles
+    static int sms = 0;
+    if (!sms) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev_of_current());
+        if (sms <= 0) sms = 148;
+    }
+    const int tiles = (T + RT_BM - 1) / RT_BM;
+    int S = 1;
+#ifndef MOE_RT_OVERSUB
+#define MOE_RT_OVERSUB 1
+#endif
+    while (S < 8 && (long long)tiles * S * 2 <= (long long)sms * MOE_RT_OVERSUB && nk / (S * 2) >= 2) S *= 2;
+    const int nkl_max = (nk + S - 1) / S;
     const size_t cap = 210 * 1024;
-    const bool resident = routing_smem_bytes(true, E, epad, nk, 4) <= cap;
+    const bool resident = routing_smem_bytes(true, E, epad, nkl_max, 4, S) <= cap;
     int nst = RT_MAX_STAGES;
-    while (nst > 2 && routing_smem_bytes(resident, E, epad, nk, nst) > cap) nst--;
-    const size_t smem = routing_smem_bytes(resident, E, epad, nk, nst);
+    while (nst > 2 && routing_smem_bytes(resident, E, epad, nkl_max, nst, S) > cap) nst--;
+    const size_t smem = routing_smem_bytes(resident, E, epad, nkl_max, nst, S);
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -361,11 +449,24 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_done[dev] = true;
     }
-    const int grid = (T + RT_BM - 1) / RT_BM;
-    if (resident)
-        routing_tc_kernel<true><<<grid, RT_THREADS, smem, s>>>(tm, w_gate, ids, weights, T, H, E, K, epad, cols, nst, nullptr);
-    else
-        routing_tc_kernel<false><<<grid, RT_THREADS, smem, s>>>(tm, w_gate, ids, weights, T, H, E, K, epad, cols, nst, nullptr);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(tiles * S);
+    lc.blockDim = dim3(RT_THREADS);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = S;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    int* no_err = nullptr;
+    cudaError_t e = resident ? cudaLaunchKernelEx(&lc, routing_tc_kernel<true>, tm, w_gate, ids, weights, T, H, E, K,
+                                                  epad, cols, nst, nkl_max, no_err)
+                             : cudaLaunchKernelEx(&lc, routing_tc_kernel<false>, tm, w_gate, ids, weights, T, H, E, K,
+                                                  epad, cols, nst, nkl_max, no_err);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
