@@ -590,7 +590,7 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
     cudaEvent_t* ev = moe::trace_begin_call();
     moe::trace_mark(ev, 0, s);
     // 1-2. routing, permutation (with its inverse), gather
-    if ((e = cudaMemsetAsync(err, 0, sizeof(int), s)) != cudaSuccess) return MOE_ERR_CUDA;
+    // the error word is cleared by the permutation launch below
     if (T > 0) {
         if ((e = moe::launch_routing(static_cast<const __half*>(x), static_cast<const __half*>(w_gate), ids,
                                      wts, (int)T, (int)H, (int)E, (int)K, s)) != cudaSuccess)
@@ -851,7 +851,7 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     unsigned int* done2 = reinterpret_cast<unsigned int*>(flags + 5);
     cudaEvent_t* ev = moe::trace_begin_call();
     moe::trace_mark(ev, 0, s);
-    if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return MOE_ERR_CUDA;
+    // the error word is cleared by the permutation launch below
     if (T > 0 && moe::launch_routing(static_cast<const __half*>(x), static_cast<const __half*>(w_gate), ids, wts,
                                      (int)T, (int)H, (int)E, (int)K, s) != cudaSuccess)
         return MOE_ERR_CUDA;

@@ -148,10 +148,8 @@ T* at(void* base, size_t off)
 int run_permute(const int32_t* ids, int64_t T, int64_t K, int64_t E, void* ws, const PermLayout& L,
                 int32_t* perm, int32_t* offsets, cudaStream_t s)
 {
-    int* err = at<int>(ws, L.err);
-    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
-    if (e != cudaSuccess) return cuda_status(e);
-    e = moe::launch_permute(ids, (int)(T * K), (int)E, at<int32_t>(ws, L.chunk_counts),
+    int* err = at<int>(ws, L.err);  // cleared by the permutation launch
+    cudaError_t e = moe::launch_permute(ids, (int)(T * K), (int)E, at<int32_t>(ws, L.chunk_counts),
                             at<int32_t>(ws, L.chunk_base), offsets, perm, nullptr, err, s);
     return cuda_status(e);
 }

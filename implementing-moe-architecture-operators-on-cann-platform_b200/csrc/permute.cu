@@ -15,8 +15,12 @@
 //   3. scatter : within a chunk, the stable rank of each entry among the entries
 //                with the same expert (warp match + per-warp prefix)
 // then a gather copies x[perm[r]/K, :] to row r of the permuted activations.
+#include <cooperative_groups.h>
+
 #include "moe_common.cuh"
 #include "moe_kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace moe {
 
@@ -125,6 +129,92 @@ gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ per
     for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
 }
 
+// The three passes in one cooperative launch (one block per chunk, every block
+// resident): histogram | grid sync | each block derives its own per-expert bases
+// from all chunk histograms (O(chunks * E) reads) and block 0 writes offsets |
+// stable scatter.  Same order as the three-kernel path, one launch instead of three.
+__global__ void __launch_bounds__(PC)
+perm_fused_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ chunk_counts,
+                  int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int32_t* __restrict__ dest,
+                  int* __restrict__ err)
+{
+    extern __shared__ int pf_smem[];
+    int* hist = pf_smem;          // [E]
+    int* base = pf_smem + E;      // [E]
+    int* wcnt = pf_smem + 2 * E;  // [32 warps][E]
+    __shared__ int bad;
+    cg::grid_group grid = cg::this_grid();
+    const int nchunks = gridDim.x;
+    if (threadIdx.x == 0) {
+        bad = 0;
+        if (blockIdx.x == 0) *err = 0;  // this call's error word starts clear (set only after the sync)
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int idx = blockIdx.x * PC + threadIdx.x;
+    for (int i = threadIdx.x; i < E; i += PC) hist[i] = 0;
+    for (int i = threadIdx.x; i < 32 * E; i += PC) wcnt[i] = 0;
+    __syncthreads();
+    int e = -1;
+    if (idx < n) {
+        e = ids[idx];
+        if (e >= 0 && e < E)
+            atomicAdd(&hist[e], 1);
+        else {
+            bad = 1;
+            e = -1;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += PC) chunk_counts[(size_t)blockIdx.x * E + i] = hist[i];
+    grid.sync();
+    if (threadIdx.x == 0 && bad) atomicOr(err, MOE_DEV_BAD_EXPERT_ID);
+    // bases: offsets[e] (all experts before e) + this expert's rows in earlier chunks
+    for (int ee = threadIdx.x; ee < E; ee += PC) {
+        int tot = 0, before = 0;
+        for (int c = 0; c < nchunks; c++) {
+            const int v = chunk_counts[(size_t)c * E + ee];
+            tot += v;
+            if (c < blockIdx.x) before += v;
+        }
+        hist[ee] = tot;  // reuse: per-expert totals
+        base[ee] = before;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive scan of the totals (E <= 256)
+        int run = 0;
+        for (int ee = 0; ee < E; ee++) {
+            const int t = hist[ee];
+            hist[ee] = run;
+            run += t;
+        }
+        if (blockIdx.x == 0) offsets[E] = run;
+    }
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += PC) {
+        base[ee] += hist[ee];
+        if (blockIdx.x == 0) offsets[ee] = hist[ee];
+    }
+    // stable rank within the chunk: warp match + per-warp prefix (as perm_scatter_kernel)
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+    if (e >= 0 && rank_in_warp == 0) wcnt[warp * E + e] = __popc(same);
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += PC) {
+        int run = 0;
+        for (int w = 0; w < 32; w++) {
+            const int c = wcnt[w * E + ee];
+            wcnt[w * E + ee] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    if (e >= 0) {
+        const int pos = base[e] + wcnt[warp * E + e] + rank_in_warp;
+        perm[pos] = idx;
+        if (dest) dest[idx] = pos;
+    }
+}
+
 // dst[r, :] = src[idx[r], :] for r < rows; one warp per row, 16-byte moves.
 __global__ void __launch_bounds__(256)
 copy_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ idx, int rows, int H,
@@ -152,6 +242,27 @@ cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_coun
                            int* err, cudaStream_t s)
 {
     const int nchunks = (n + PC - 1) / PC;
+    // one cooperative launch when every chunk's block can be resident at once
+    static int capacity[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t fsmem = (size_t)(34 * E) * sizeof(int);
+    if (dev >= 0 && dev < 64 && capacity[dev] == 0) {
+        int per_sm = 0, sms = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, perm_fused_kernel, PC, 34 * 256 * sizeof(int));
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        capacity[dev] = per_sm * sms > 0 ? per_sm * sms : -1;
+    }
+    if (nchunks > 0 && dev >= 0 && dev < 64 && nchunks <= capacity[dev]) {
+        void* args[] = {(void*)&ids, (void*)&n, (void*)&E, (void*)&chunk_counts, (void*)&offsets,
+                        (void*)&perm, (void*)&dest, (void*)&err};
+        cudaError_t e = cudaLaunchCooperativeKernel((const void*)perm_fused_kernel, dim3(nchunks), dim3(PC), args,
+                                                    fsmem, s);
+        if (e == cudaSuccess) return cudaSuccess;
+        cudaGetLastError();  // fall back to the three-kernel path
+    }
+    cudaError_t me = cudaMemsetAsync(err, 0, sizeof(int), s);
+    if (me != cudaSuccess) return me;
     if (nchunks > 0) {
         perm_count_kernel<<<nchunks, PC, E * sizeof(int), s>>>(ids, n, E, chunk_counts, err);
     }
