@@ -145,6 +145,33 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
     // flight per thread, and scatter each half to (row n = expert, k = h % 64) of the
     // tile of k-block h / 64 (tile_of(kb) gives its address).
     auto b_fill_rows = [&](int h_begin, int h_end, auto tile_of) {
+        if ((E & 7) == 0 && ((h_end - h_begin) & 7) == 0) {
+            // 8 h x 8 experts per step: eight 16-byte loads (one per h row), an 8x8
+            // transpose of 16-bit values in registers, eight 16-byte swizzled stores
+            const int hg = (h_end - h_begin) >> 3, eg = E >> 3;
+            for (int b = tid; b < hg * eg; b += RT_THREADS) {
+                const int h0 = h_begin + (b / eg) * 8, e0 = (b % eg) * 8;
+                uint4 in[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    in[j] = __ldg(reinterpret_cast<const uint4*>(w_gate + (size_t)(h0 + j) * E + e0));
+                uint8_t* bt = tile_of(h0 / RT_BK);
+                const int k = h0 % RT_BK;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {  // expert e0+j: halves j of rows h0..h0+7
+                    const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
+                    uint32_t w[4];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const uint32_t* a = reinterpret_cast<const uint32_t*>(&in[2 * q]);
+                        const uint32_t* c = reinterpret_cast<const uint32_t*>(&in[2 * q + 1]);
+                        w[q] = __byte_perm(a[j >> 1], c[j >> 1], sel);
+                    }
+                    *reinterpret_cast<uint4*>(bt + sw128_offset(e0 + j, k)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            return;
+        }
         const uint4* src = reinterpret_cast<const uint4*>(w_gate + (size_t)h_begin * E);
         const int nvec = ((h_end - h_begin) * E) >> 3;  // H*E and 64*E are multiples of 8
         for (int v0 = tid; v0 < nvec; v0 += 8 * RT_THREADS) {
@@ -347,35 +374,54 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
         }
     }
     RT_STAMP(4)
-    // softmax + top-K for this thread's token, reference order (moe_cpu_sim.cpp:211-243)
+    // softmax + top-K for this thread's token (moe_cpu_sim.cpp:211-243) in one pass:
+    // the exp-sum in expert order as the reference sums it, and a stable top-8 of the
+    // exps kept in registers (strict '>' keeps the lower id ahead on equal values).
+    // Only the selected probabilities are divided, p = e / sum, as the reference
+    // computes them; ordering by e instead of e / sum can differ only where the
+    // division rounds two different exps to one probability (a near tie).
     const int t = t0 + r;
     if (t < T) {
-        float* l = lg + (size_t)r * pitch;
+        const float* l = lg + (size_t)r * pitch;
         float maxv = -1e30f;
         for (int i = 0; i < E; i++) maxv = l[i] > maxv ? l[i] : maxv;
         float sum = 0.0f;
+        float tv[8];
+        int ti[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            tv[j] = -1.0f;
+            ti[j] = 0;
+        }
         for (int i = 0; i < E; i++) {
-            const float pe = expf(l[i] - maxv);
-            l[i] = pe;
-            sum += pe;
-        }
-        for (int i = 0; i < E; i++) l[i] = l[i] / sum;
-        float wsum = 0.0f;
-        float selp[8];
-        for (int k = 0; k < K; k++) {  // K passes; strict '>' keeps the lower id on ties
-            int best = -1;
-            float bv = 0.0f;
-            for (int i = 0; i < E; i++) {
-                const float v = l[i];
-                if (v < 0.0f) continue;
-                if (best < 0 || v > bv) { best = i; bv = v; }
+            float cv = expf(l[i] - maxv);
+            sum += cv;
+            int ci = i;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (cv > tv[j]) {
+                    const float fv = tv[j];
+                    const int fi = ti[j];
+                    tv[j] = cv;
+                    ti[j] = ci;
+                    cv = fv;
+                    ci = fi;
+                }
             }
-            expert_ids[(size_t)t * K + k] = best;
-            l[best] = -1.0f;  // selected: excluded from the next passes
-            selp[k] = bv;
-            wsum += bv;  // selection order, as the reference's wSum (moe_cpu_sim.cpp:236-240)
         }
-        for (int k = 0; k < K; k++) weights[(size_t)t * K + k] = __float2half_rn(selp[k] / wsum);
+        float wsum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < K) {
+                tv[j] = tv[j] / sum;  // the selected probabilities
+                wsum += tv[j];        // selection order, as the reference's wSum (moe_cpu_sim.cpp:236-240)
+            }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < K) {
+                expert_ids[(size_t)t * K + j] = ti[j];
+                weights[(size_t)t * K + j] = __float2half_rn(tv[j] / wsum);
+            }
     }
     __syncthreads();
     RT_STAMP(5)
@@ -432,8 +478,10 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
 #define MOE_RT_OVERSUB 1
 #endif
     while (S < 8 && (long long)tiles * S * 2 <= (long long)sms * MOE_RT_OVERSUB && nk / (S * 2) >= 2) S *= 2;
-    const int nkl_max = (nk + S - 1) / S;
     const size_t cap = 210 * 1024;
+    // a wider split when it lets each CTA keep its slice of w_gate^T resident (large E)
+    while (S < 8 && routing_smem_bytes(true, E, epad, (nk + S - 1) / S, 4, S) > cap && nk / (S * 2) >= 2) S *= 2;
+    const int nkl_max = (nk + S - 1) / S;
     const bool resident = routing_smem_bytes(true, E, epad, nkl_max, 4, S) <= cap;
     int nst = RT_MAX_STAGES;
     while (nst > 2 && routing_smem_bytes(resident, E, epad, nkl_max, nst, S) > cap) nst--;
