@@ -899,3 +899,29 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
 }
 
 }  // namespace
+
+extern "C" int MoeEpSelfTestWaitTimeout(int* code)
+{
+    // The expert-parallel kernels' bounded wait, on a flag that nothing sets: after
+    // its time limit the kernel records the error bit and returns, and the context
+    // stays usable.  Used by the failure-detection test; no GPU fault involved.
+    if (!code) return MOE_ERR_NULL_POINTER;
+    unsigned long long* flag = nullptr;
+    int* err = nullptr;
+    if (cudaMalloc(&flag, sizeof(*flag)) != cudaSuccess) return MOE_ERR_CUDA;
+    if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) {
+        cudaFree(flag);
+        return MOE_ERR_CUDA;
+    }
+    cudaMemset(flag, 0, sizeof(*flag));
+    cudaMemset(err, 0, sizeof(int));
+    ep_p2p_wait_kernel<<<1, 32>>>(flag, 1ull, err, EP_ERR_WAIT_ROWS);
+    cudaError_t e = cudaDeviceSynchronize();
+    int v = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    cudaFree(err);
+    if (e != cudaSuccess) return MOE_ERR_CUDA;
+    *code = v;
+    return MOE_OK;
+}

@@ -159,6 +159,12 @@ int MoeEpLayerForward(MoeEpContext* ctx, const void* x, const void* w_gate,
 int MoeEpPlan(const int32_t* sendCounts, const int32_t* recvCounts, int nranks, int expertsPerRank,
               int32_t* sendOff, int32_t* recvOff, int32_t* expertOff, int32_t* segments);
 
+/* Failure-detection self-test (no reference counterpart): runs the expert-parallel
+ * kernels' bounded flag wait on a flag that nothing sets.  The wait gives up after
+ * its limit (about 2 s) and records its error bit (128) in *code; the context stays
+ * usable.  Returns MOE_OK or MOE_ERR_CUDA. */
+int MoeEpSelfTestWaitTimeout(int* code);
+
 /* ------------------------------------------------------------------ permutation */
 
 /* The token permutation inside MoeExpertFFN, exposed on its own.  Replaces the
@@ -173,8 +179,10 @@ int MoePermute(const int32_t* expert_ids, int32_t* perm, int32_t* expert_offsets
 /* ------------------------------------------------------------------ diagnostics */
 
 /* Synchronises `stream` and reads the device error word of a MoeExpertFFN,
- * MoeLayerForward or MoePermute workspace into *code (0 = none; bit 1 = expert
- * id out of range, bits 2/4/8 = a bounded wait timed out).  Returns MOE_OK or
+ * MoeLayerForward, MoePermute or MoeEpLayerForward workspace into *code (0 = none;
+ * 1 = expert id out of range; 2/4/8 = a grouped-GEMM wait timed out; expert
+ * parallel: 64/128/256 = the counts / rows / returned-rows flag wait timed out,
+ * 512 = more rows than the workspace's maxRecvRows).  Returns MOE_OK or
  * MOE_ERR_CUDA. */
 int MoeGetDeviceError(const void* workspace, int* code, void* stream);
 

@@ -142,3 +142,20 @@ def test_ep_multi_gpu_matches_layer(shape, path):
         p.join(timeout=120)
     for rank, eq1, eq2, err in res:
         assert eq1 and eq2, (rank, err)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(moe):
+    """A device wait on a flag nothing sets gives up, reports its error bit, and
+    the CUDA context keeps working afterwards."""
+    import ctypes
+
+    L = moe.lib()
+    L.MoeEpSelfTestWaitTimeout.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    code = ctypes.c_int(0)
+    assert L.MoeEpSelfTestWaitTimeout(ctypes.byref(code)) == 0
+    assert code.value == 128  # rows-flag wait timed out
+    T, H, E, K, I = 64, 128, 4, 2, 128
+    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, 1)
+    y = moe.moe_layer_forward(x, wg, ew, K)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all()
