@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(256)
 combine_kernel(const __half* __restrict__ expert_out, const __half* __restrict__ weights,
                __half* __restrict__ y, int T, int H, int K)
 {
+    pdl_wait();  // expert_out comes from the down GEMM (a no-op when launched plainly)
     const int vpr = H >> 3;  // 16-byte vectors per row
     const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (v >= (long long)T * vpr) return;
@@ -94,7 +95,8 @@ cudaError_t launch_combine(const __half* expert_out, const __half* weights, __ha
     long long nv = (long long)T * (H >> 3);
     if (nv == 0) return cudaSuccess;
     int grid = (int)((nv + 255) / 256);
-    combine_kernel<<<grid, 256, 0, s>>>(expert_out, weights, y, T, H, K);
+    cudaError_t e = launch_pdl(combine_kernel, dim3(grid), dim3(256), 0, s, expert_out, weights, y, T, H, K);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -185,6 +185,8 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
+    pdl_trigger();
+    pdl_wait();  // offsets, A rows (and perm) come from the previous launches
     if (warp == 2) {  // tile prefix: tiles per expert = ceil(rows/128) * n_tiles
         if (lane == 0) {
             int run = 0;
@@ -504,7 +506,8 @@ cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, c
     a.b_hi_delta = I;
     a.out_ld = I;
     const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
-    ffn_gemm_kernel<MODE_SWIGLU><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
+    e = launch_pdl(ffn_gemm_kernel<MODE_SWIGLU>, dim3(grid), dim3(GM_THREADS), gemm_smem_bytes(), s, ta, tb, a);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -534,7 +537,8 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
     a.b_hi_delta = 128;
     a.out_ld = H;
     const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
-    ffn_gemm_kernel<MODE_DOWN><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
+    e = launch_pdl(ffn_gemm_kernel<MODE_DOWN>, dim3(grid), dim3(GM_THREADS), gemm_smem_bytes(), s, ta, tb, a);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

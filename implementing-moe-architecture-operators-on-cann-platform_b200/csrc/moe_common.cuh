@@ -98,6 +98,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// ------------------------------------------------------------------ dependent launch
+// Programmatic dependent launch: a kernel lets the next kernel of the stream start
+// its prologue early (pdl_trigger), and that kernel waits for this one's results
+// before reading them (pdl_wait).  Both are no-ops without the launch attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm)
 {

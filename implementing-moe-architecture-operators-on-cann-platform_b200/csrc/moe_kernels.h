@@ -8,6 +8,25 @@
 
 namespace moe {
 
+// Launches `kernel` with programmatic stream serialisation allowed: it may start
+// while the previous kernel of the stream drains, and waits for it with pdl_wait().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args)
+{
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, static_cast<KArgs>(args)...);
+}
+
 enum GemmMode { MODE_SWIGLU = 0, MODE_DOWN = 1, MODE_DOWN_PTR = 2 };
 
 cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights,

@@ -119,6 +119,8 @@ gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ per
                    const int32_t* __restrict__ offsets, int E, int K, int H, int rows_cap,
                    __half* __restrict__ xp)
 {
+    pdl_trigger();
+    pdl_wait();  // perm / offsets come from the permutation launch
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= rows_cap || r >= offsets[E]) return;
@@ -143,6 +145,7 @@ perm_fused_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __rest
     int* base = pf_smem + E;      // [E]
     int* wcnt = pf_smem + 2 * E;  // [32 warps][E]
     __shared__ int bad;
+    pdl_trigger();
     cg::grid_group grid = cg::this_grid();
     const int nchunks = gridDim.x;
     if (threadIdx.x == 0) {
@@ -279,7 +282,9 @@ cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32
                                int K, int H, int rows_cap, __half* xp, cudaStream_t s)
 {
     if (rows_cap == 0) return cudaSuccess;
-    gather_rows_kernel<<<(rows_cap + 7) / 8, 256, 0, s>>>(x, perm, offsets, E, K, H, rows_cap, xp);
+    cudaError_t e = launch_pdl(gather_rows_kernel, dim3((rows_cap + 7) / 8), dim3(256), 0, s, x, perm, offsets, E,
+                               K, H, rows_cap, xp);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
