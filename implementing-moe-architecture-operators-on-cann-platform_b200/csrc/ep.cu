@@ -873,7 +873,7 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 3, s);
     cudaError_t e = moe::launch_gemm_swiglu(rows_local, static_cast<const __half*>(ewl), expoff, hbuf, err, (int)R,
-                                            (int)H, El, (int)I, 0, s);
+                                            (int)H, El, (int)I, 0, s, (int)(T * K));
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 4, s);
@@ -882,7 +882,7 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     e = moe::launch_gemm_down_ptr(hbuf, static_cast<const __half*>(ewl), expoff, row_ptr, done2,
                                   reinterpret_cast<unsigned long long* const*>(
                                       reinterpret_cast<const uint8_t*>(dp) + offsetof(EpPeers, ret_flag)),
-                                  n, err, (int)R, (int)H, El, (int)I, s);
+                                  n, err, (int)R, (int)H, El, (int)I, s, (int)(T * K));
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 5, s);

@@ -25,8 +25,14 @@
 // same time share one weight tile in L2 and every weight byte comes from HBM once.
 // The tile list is derived on the device from offsets[] (no host sync).
 //
-// No cluster launch and no cluster-broadcast loads are used: the same kernel runs on every
-// rank of the expert-parallel path.
+// Paired mode (PAIR=1, large experts): a 2-CTA cluster shares M=256 cta_group::2
+// UMMAs; the leader CTA issues them and owns the barriers they wait on, and each
+// CTA loads its own half of A and B into its own shared memory.  No load is
+// broadcast to several CTAs, so the same kernel runs on every rank of the
+// expert-parallel path.
+#include <cstdio>
+#include <cstdlib>
+
 #include "moe_common.cuh"
 #include "moe_kernels.h"
 
@@ -80,9 +86,26 @@ struct GemmArgs {
     int npeers;
 };
 
+// Paired-CTA variant (PAIR=1): a 2-CTA cluster runs one 256-row tile with M=256
+// cta_group::2 UMMAs.  Each CTA stages its own 128 rows of A and one half (128
+// rows) of the tile's 256 B rows, so every SM reads 32 KB of shared memory per k
+// block instead of 48 KB; that leaves room for deeper pipelines.
+#ifndef MOE_GEMM_PAIR_STAGES
+#define MOE_GEMM_PAIR_STAGES 6
+#endif
+constexpr int GM_MAX_STAGES = 8;
+
+template <int PAIR>
+struct GemmCfg {
+    static constexpr int STAGES = PAIR ? MOE_GEMM_PAIR_STAGES : GM_STAGES;
+    static constexpr int STAGE_BYTES = PAIR ? GM_A_BYTES + GM_BHALF_BYTES : GM_STAGE_BYTES;
+    static constexpr int ROWS = PAIR ? 2 * GM_BM : GM_BM;  // rows of one tile (over the pair)
+};
+static_assert(GemmCfg<0>::STAGES <= GM_MAX_STAGES && GemmCfg<1>::STAGES <= GM_MAX_STAGES, "stages");
+
 struct GemmSmemTail {
-    uint64_t full[GM_STAGES];
-    uint64_t empty[GM_STAGES];
+    uint64_t full[GM_MAX_STAGES];
+    uint64_t empty[GM_MAX_STAGES];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
@@ -96,11 +119,13 @@ struct GemmSmemTail {
 constexpr int GM_STG_ROW = 80;
 constexpr int GM_STG_BYTES = 4 * 32 * GM_STG_ROW;
 
+template <int PAIR>
 __host__ __device__ constexpr size_t gemm_smem_bytes()
 {
-    return 1024 + (size_t)GM_STAGES * GM_STAGE_BYTES + ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) +
-           GM_STG_BYTES;
+    return 1024 + (size_t)GemmCfg<PAIR>::STAGES * GemmCfg<PAIR>::STAGE_BYTES +
+           ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) + GM_STG_BYTES;
 }
+static_assert(gemm_smem_bytes<0>() <= 227 * 1024 && gemm_smem_bytes<1>() <= 227 * 1024, "smem");
 
 // Stores one 32-column chunk (64 bytes) of each of the warp's 32 rows.  Each
 // thread parks its row's chunk in shared memory (rows padded to 80 bytes so the
@@ -136,8 +161,9 @@ __device__ __forceinline__ void epi_warp_store(uint8_t* stg_warp, int lane, cons
     __syncwarp();
 }
 
-// Maps a CTA-visited tile index to (expert, m tile, n tile).  Tile indices a
-// CTA visits only grow, so the expert cursor only moves forward.
+// Maps a tile index to (expert, m tile, n tile); m tiles are `ROWS` rows.  Tile
+// indices a CTA visits only grow, so the expert cursor only moves forward.
+template <int ROWS>
 struct TileCursor {
     int e = 0;
     __device__ __forceinline__ void decode(const int* prefix, const int32_t* offsets, int n_tiles,
@@ -145,7 +171,7 @@ struct TileCursor {
     {
         while (tile >= prefix[e + 1]) e++;
         const int cnt = offsets[e + 1] - offsets[e];
-        const int mts = (cnt + GM_BM - 1) / GM_BM;
+        const int mts = (cnt + ROWS - 1) / ROWS;
         const int local = tile - prefix[e];
         nt = local / mts;
         mt = local - nt * mts;
@@ -153,29 +179,39 @@ struct TileCursor {
     }
 };
 
-template <int MODE>
+template <int MODE, int PAIR>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmArgs args)
 {
+    using Cfg = GemmCfg<PAIR>;
+    constexpr int STAGES = Cfg::STAGES;
+    constexpr int STAGE_BYTES = Cfg::STAGE_BYTES;
+    constexpr int ROWS = Cfg::ROWS;
     extern __shared__ uint8_t gm_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(gm_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + GM_STAGES * GM_STAGE_BYTES);
+    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + STAGES * STAGE_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int E = args.E;
     const int32_t* __restrict__ offsets = args.offsets;
+    // Pair mode: rank 0 of the cluster is the leader (issues the UMMAs and owns the
+    // barriers the UMMAs wait on); `unit` numbers the pairs.
+    const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = crank == 0u;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int nunits = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < GM_STAGES; s++) {
+        for (int s = 0; s < STAGES; s++) {
             mbar_init(smem_u32(&tail->full[s]), 1);
             mbar_init(smem_u32(&tail->empty[s]), 1);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(smem_u32(&tail->tfull[a]), 1);
-            mbar_init(smem_u32(&tail->tempty[a]), 128);
+            mbar_init(smem_u32(&tail->tempty[a]), PAIR ? 8 : 4);  // one arrival per epilogue warp
         }
         mbar_init(smem_u32(&tail->drain), 1);
         tail->abort_flag = 0;
@@ -187,23 +223,31 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
     pdl_trigger();
     pdl_wait();  // offsets, A rows (and perm) come from the previous launches
-    if (warp == 2) {  // tile prefix: tiles per expert = ceil(rows/128) * n_tiles
+    if (warp == 2) {  // tile prefix: tiles per expert = ceil(rows/ROWS) * n_tiles
         if (lane == 0) {
             int run = 0;
             for (int e = 0; e < E; e++) {
                 tail->tile_prefix[e] = run;
                 const int cnt = offsets[e + 1] - offsets[e];
-                run += ((cnt + GM_BM - 1) / GM_BM) * args.n_tiles;
+                run += ((cnt + ROWS - 1) / ROWS) * args.n_tiles;
             }
             tail->tile_prefix[E] = run;
         }
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(&tail->tmem_base), GM_TMEM_COLS);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(smem_u32(&tail->tmem_base), GM_TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(&tail->tmem_base), GM_TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR)
+        cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
+    else
+        __syncthreads();
     tc_fence_after();
 
     const uint32_t tmem_base = tail->tmem_base;
@@ -220,82 +264,127 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 #else
             const uint64_t pol_b = l2_policy_evict_first();
 #endif
-            TileCursor cur;
+            TileCursor<ROWS> cur;
             uint32_t it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+            for (int tile = unit; ok && tile < total_tiles; tile += nunits) {
                 int e, mt, nt;
                 cur.decode(tail->tile_prefix, offsets, args.n_tiles, tile, e, mt, nt);
-                const int a_row = offsets[e] + mt * GM_BM;
+                const int a_row = offsets[e] + mt * ROWS + (int)crank * GM_BM;
                 const int b_lo = e * args.b_rows_per_expert + args.b_seg + nt * args.b_nstep;
                 const int b_hi = b_lo + args.b_hi_delta;
                 for (int kb = 0; kb < nk; kb++, it++) {
-                    const int s = it % GM_STAGES;
-                    const uint32_t par = ((it / GM_STAGES) & 1u) ^ 1u;
-                    if (!mbar_wait_bounded(smem_u32(&tail->empty[s]), par, args.err,
-                                           MOE_DEV_WAIT_TIMEOUT_TMA, abort_flag)) {
+                    const int s = it % STAGES;
+                    const uint32_t par = ((it / STAGES) & 1u) ^ 1u;
+                    const bool got = PAIR ? mbar_wait_bounded_cluster(smem_u32(&tail->empty[s]), par, args.err,
+                                                                      MOE_DEV_WAIT_TIMEOUT_TMA, abort_flag)
+                                          : mbar_wait_bounded(smem_u32(&tail->empty[s]), par, args.err,
+                                                              MOE_DEV_WAIT_TIMEOUT_TMA, abort_flag);
+                    if (!got) {
                         ok = false;
                         break;
                     }
                     const uint32_t full = smem_u32(&tail->full[s]);
-                    uint8_t* st = smem + s * GM_STAGE_BYTES;
-                    mbar_arrive_expect_tx(full, GM_STAGE_BYTES);
-                    tma_load_2d(smem_u32(st), &tmA, full, kb * GM_BK, a_row, pol_a);
-                    tma_load_2d(smem_u32(st + GM_A_BYTES), &tmB, full, kb * GM_BK, b_lo, pol_b);
-                    tma_load_2d(smem_u32(st + GM_A_BYTES + GM_BHALF_BYTES), &tmB, full, kb * GM_BK,
-                                b_hi, pol_b);
+                    uint8_t* st = smem + s * STAGE_BYTES;
+                    if (PAIR) {
+                        // Both CTAs' copies complete on the leader's barrier; the leader
+                        // expects the bytes of both.
+                        const uint32_t full_leader = mapa_shared(full, 0);
+                        if (leader) mbar_arrive_expect_tx(full, 2 * STAGE_BYTES);
+                        tma_load_2d_pair(smem_u32(st), &tmA, full_leader, kb * GM_BK, a_row, pol_a);
+                        tma_load_2d_pair(smem_u32(st + GM_A_BYTES), &tmB, full_leader, kb * GM_BK,
+                                         leader ? b_lo : b_hi, pol_b);
+                    } else {
+                        mbar_arrive_expect_tx(full, STAGE_BYTES);
+                        tma_load_2d(smem_u32(st), &tmA, full, kb * GM_BK, a_row, pol_a);
+                        tma_load_2d(smem_u32(st + GM_A_BYTES), &tmB, full, kb * GM_BK, b_lo, pol_b);
+                        tma_load_2d(smem_u32(st + GM_A_BYTES + GM_BHALF_BYTES), &tmB, full, kb * GM_BK,
+                                    b_hi, pol_b);
+                    }
                 }
             }
-            if (!ok) {
-                // Unwinding after a timeout: wait (bounded) until the copies this
-                // thread issued into the ring have landed before the CTA exits.
-                const uint32_t first = it > GM_STAGES ? it - GM_STAGES : 0;
+            if (!ok && leader) {
+                // Unwinding after a timeout: wait (bounded) until the copies issued into
+                // the ring have landed before the CTA exits.  In pair mode the leader's
+                // barriers count the copies of both CTAs, and the peer stays resident
+                // until the leader reaches the closing cluster barrier.
+                const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
                 for (uint32_t j = first; j < it; j++) {
                     const uint64_t t0 = global_timer_ns();
-                    while (!mbar_try_wait(smem_u32(&tail->full[j % GM_STAGES]), (j / GM_STAGES) & 1u))
+                    while (!(PAIR ? mbar_try_wait_cluster(smem_u32(&tail->full[j % STAGES]), (j / STAGES) & 1u)
+                                  : mbar_try_wait(smem_u32(&tail->full[j % STAGES]), (j / STAGES) & 1u)))
                         if (global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) break;
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_f16_f32(GM_BM, GM_BN);
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = umma_idesc_f16_f32(ROWS, GM_BN);
             uint32_t it = 0, lt = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, lt++) {
+            for (int tile = unit; ok && tile < total_tiles; tile += nunits, lt++) {
                 const uint32_t acc = lt & 1u;
-                if (!mbar_wait_bounded(smem_u32(&tail->tempty[acc]), ((lt >> 1) & 1u) ^ 1u, args.err,
-                                       MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                const uint32_t tpar = ((lt >> 1) & 1u) ^ 1u;
+                const bool free_acc =
+                    PAIR ? mbar_wait_bounded_cluster(smem_u32(&tail->tempty[acc]), tpar, args.err,
+                                                     MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)
+                         : mbar_wait_bounded(smem_u32(&tail->tempty[acc]), tpar, args.err, MOE_DEV_WAIT_TIMEOUT_MMA,
+                                             abort_flag);
+                if (!free_acc) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * GM_BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
-                    const int s = it % GM_STAGES;
-                    if (!mbar_wait_bounded(smem_u32(&tail->full[s]), (it / GM_STAGES) & 1u, args.err,
-                                           MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)) {
+                    const int s = it % STAGES;
+                    const uint32_t fpar = (it / STAGES) & 1u;
+                    const bool got = PAIR ? mbar_wait_bounded_cluster(smem_u32(&tail->full[s]), fpar, args.err,
+                                                                      MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag)
+                                          : mbar_wait_bounded(smem_u32(&tail->full[s]), fpar, args.err,
+                                                              MOE_DEV_WAIT_TIMEOUT_MMA, abort_flag);
+                    if (!got) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + s * GM_STAGE_BYTES);
+                    const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
                     const uint32_t b_addr = a_addr + GM_A_BYTES;
 #pragma unroll
                     for (int k = 0; k < GM_BK / 16; k++) {
                         // advancing K by 16 fp16 = 32 bytes inside the 128-byte swizzle row
-                        umma_f16_ss(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                                    idesc, (kb | k) != 0);
+                        if (PAIR)
+                            umma_f16_ss_pair(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                             idesc, (kb | k) != 0);
+                        else
+                            umma_f16_ss(d, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                                        idesc, (kb | k) != 0);
                     }
-                    umma_commit(smem_u32(&tail->empty[s]));  // frees the stage when these MMAs finish
+                    // frees the stage (in both CTAs of a pair) when these MMAs finish
+                    if (PAIR) {
+                        umma_commit_pair(smem_u32(&tail->empty[s]));
+                        umma_commit_pair(mapa_shared(smem_u32(&tail->empty[s]), 1));
+                    } else {
+                        umma_commit(smem_u32(&tail->empty[s]));
+                    }
                 }
-                if (ok) umma_commit(smem_u32(&tail->tfull[acc]));  // accumulator ready
+                if (ok) {  // accumulator ready
+                    if (PAIR) {
+                        umma_commit_pair(smem_u32(&tail->tfull[acc]));
+                        umma_commit_pair(mapa_shared(smem_u32(&tail->tfull[acc]), 1));
+                    } else {
+                        umma_commit(smem_u32(&tail->tfull[acc]));
+                    }
+                }
             }
-            // Make sure no MMA of this CTA is still running before TMEM is freed.
-            umma_commit(smem_u32(&tail->drain));
+            // Make sure no MMA of this CTA (pair) is still running before TMEM is freed.
+            if (PAIR)
+                umma_commit_pair(smem_u32(&tail->drain));
+            else
+                umma_commit(smem_u32(&tail->drain));
             const uint64_t t0 = global_timer_ns();
-            while (!mbar_try_wait(smem_u32(&tail->drain), 0))
+            while (!(PAIR ? mbar_try_wait_cluster(smem_u32(&tail->drain), 0) : mbar_try_wait(smem_u32(&tail->drain), 0)))
                 if (global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) {
                     atomicOr(args.err, MOE_DEV_WAIT_TIMEOUT_MMA);
                     break;
@@ -304,27 +393,32 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     } else {
         // ---------------------------------------------------------------- epilogue
         const int q = warp & 3;            // TMEM lane quarter this warp may access
-        const int r = q * 32 + lane;       // row inside the tile
+        const int r = q * 32 + lane;       // row inside this CTA's 128 rows of the tile
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        uint8_t* stg_warp = smem + GM_STAGES * GM_STAGE_BYTES + ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) +
+        uint8_t* stg_warp = smem + STAGES * STAGE_BYTES + ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) +
                             (size_t)(warp - 2) * 32 * GM_STG_ROW;
-        TileCursor cur;
+        // In pair mode every epilogue warp of both CTAs releases the leader's accumulator.
+        const uint32_t tempty_bar0 = PAIR ? mapa_shared(smem_u32(&tail->tempty[0]), 0) : smem_u32(&tail->tempty[0]);
+        TileCursor<ROWS> cur;
         uint32_t lt = 0;
-        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, lt++) {
+        for (int tile = unit; tile < total_tiles; tile += nunits, lt++) {
             int e, mt, nt;
             cur.decode(tail->tile_prefix, offsets, args.n_tiles, tile, e, mt, nt);
             const uint32_t acc = lt & 1u;
-            if (!mbar_wait_bounded(smem_u32(&tail->tfull[acc]), (lt >> 1) & 1u, args.err,
-                                   MOE_DEV_WAIT_TIMEOUT_EPI, abort_flag))
-                break;
+            const uint32_t tpar = (lt >> 1) & 1u;
+            const bool ready = PAIR ? mbar_wait_bounded_cluster(smem_u32(&tail->tfull[acc]), tpar, args.err,
+                                                                MOE_DEV_WAIT_TIMEOUT_EPI, abort_flag)
+                                    : mbar_wait_bounded(smem_u32(&tail->tfull[acc]), tpar, args.err,
+                                                        MOE_DEV_WAIT_TIMEOUT_EPI, abort_flag);
+            if (!ready) break;
             tc_fence_after();
-            const int row0 = offsets[e] + mt * GM_BM;
-            const int rows = min(GM_BM, offsets[e + 1] - row0);
+            const int row0 = offsets[e] + mt * ROWS + (int)crank * GM_BM;
+            const int rows = min(GM_BM, offsets[e + 1] - row0);  // <= 0: this CTA's half is empty
             const bool valid = r < rows;
             const uint32_t tbase = tmem_base + acc * GM_BN + lane_off;
             if (MODE == MODE_SWIGLU) {
                 const int col0 = nt * 128;
-                __half* dst = args.out + (size_t)(row0 + r) * args.out_ld + col0;
+                __half* dst = valid ? args.out + (size_t)(row0 + r) * args.out_ld + col0 : nullptr;
 #pragma unroll 1
                 for (int j = 0; j < 4; j++) {
                     uint32_t g[32], u[32];
@@ -388,16 +482,31 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 }
             }
             tc_fence_before();
-            mbar_arrive(smem_u32(&tail->tempty[acc]));
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t bar = tempty_bar0 + acc * (uint32_t)sizeof(uint64_t);
+                if (PAIR)
+                    mbar_arrive_cluster(bar);
+                else
+                    mbar_arrive(bar);
+            }
         }
     }
 
     if (MODE == MODE_DOWN_PTR) __threadfence_system();  // this thread's (peer) row stores
-    __syncthreads();
+    // Pair mode: neither CTA frees TMEM or exits while the other may still address it.
+    __syncwarp();
+    if (PAIR)
+        cluster_sync_all();
+    else
+        __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, GM_TMEM_COLS);
+        if (PAIR)
+            tmem_dealloc_pair(tmem_base, GM_TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, GM_TMEM_COLS);
     }
     if (MODE == MODE_DOWN_PTR && threadIdx.x == 0) {
         __threadfence_system();
@@ -458,16 +567,16 @@ static int sm_count()
     return n[dev];
 }
 
-template <int MODE>
+template <int MODE, int PAIR>
 static cudaError_t set_gemm_attr()
 {
     static bool done[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_kernel<MODE>,
+    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_kernel<MODE, PAIR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemm_smem_bytes());
+                                         (int)gemm_smem_bytes<PAIR>());
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
 }
@@ -480,17 +589,108 @@ int grid_for(int rows_cap, int E, int n_tiles, int max_ctas)
     return (int)(upper < sms ? (upper > 0 ? upper : 1) : sms);
 }
 
+// Paired-CTA tiles pay off when experts hold many 256-row tiles: the pair halves
+// each SM's shared-memory traffic, but an expert's rows are padded to 256 instead
+// of 128.  MOE_GEMM_PAIR=0/1 forces the choice; otherwise pairs are used from
+// 1536 rows per expert on average (measured: faster at 1536 and 2048 rows per
+// expert, slower at 512).
+static bool use_pair(int rows_cap, int E)
+{
+    static int forced = -2;
+    if (forced == -2) {
+        const char* v = getenv("MOE_GEMM_PAIR");
+        forced = (v && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
+    }
+    if (forced >= 0) return forced == 1;
+    return E > 0 && rows_cap / E >= 1536;
+}
+
+template <int MODE, int PAIR>
+static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int rows_cap,
+                              int max_ctas, bool pdl, cudaStream_t s)
+{
+    cudaError_t e = set_gemm_attr<MODE, PAIR>();
+    if (e != cudaSuccess) return e;
+    int grid;
+    if (PAIR) {
+        constexpr int R = GemmCfg<1>::ROWS;
+        const long long upper = (long long)a.n_tiles * ((rows_cap + R - 1) / R + a.E);
+        // Co-resident pairs: a pair needs two free SMs of one GPC, so GPCs with an odd
+        // number of usable SMs leave one idle; a grid of sms/2 pairs would run a tail.
+        static int resident[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        int pairs_cap = (dev >= 0 && dev < 64) ? resident[dev] : 0;
+        if (pairs_cap <= 0) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3(2 * (sm_count() / 2));
+            q.blockDim = dim3(GM_THREADS);
+            q.dynamicSmemBytes = gemm_smem_bytes<PAIR>();
+            cudaLaunchAttribute ca;
+            ca.id = cudaLaunchAttributeClusterDimension;
+            ca.val.clusterDim.x = 2;
+            ca.val.clusterDim.y = 1;
+            ca.val.clusterDim.z = 1;
+            q.attrs = &ca;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, ffn_gemm_kernel<MODE, PAIR>, &q) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = sm_count() / 2;
+            }
+            if (getenv("MOE_GEMM_PAIR_DEBUG")) fprintf(stderr, "moe: %d co-resident CTA pairs\n", n);
+            pairs_cap = n;
+            if (dev >= 0 && dev < 64) resident[dev] = n;
+        }
+        if (max_ctas > 0 && max_ctas / 2 < pairs_cap) pairs_cap = max_ctas / 2;
+        if (pairs_cap < 1) pairs_cap = 1;
+        grid = 2 * (int)(upper < pairs_cap ? (upper > 0 ? upper : 1) : pairs_cap);
+    } else {
+        grid = grid_for(rows_cap, a.E, a.n_tiles, max_ctas);
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(grid);
+    lc.blockDim = dim3(GM_THREADS);
+    lc.dynamicSmemBytes = gemm_smem_bytes<PAIR>();
+    lc.stream = s;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (PAIR) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 2;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    lc.attrs = at;
+    lc.numAttrs = na;
+    e = cudaLaunchKernelEx(&lc, ffn_gemm_kernel<MODE, PAIR>, ta, tb, a);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+template <int MODE>
+static cudaError_t launch_ffn_any(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int rows_cap,
+                                  int rows_hint, int max_ctas, bool pdl, cudaStream_t s)
+{
+    if (use_pair(rows_hint >= 0 ? rows_hint : rows_cap, a.E)) return launch_ffn<MODE, 1>(ta, tb, a, rows_cap, max_ctas, pdl, s);
+    return launch_ffn<MODE, 0>(ta, tb, a, rows_cap, max_ctas, pdl, s);
+}
+
 // GEMM1: h[rows, I] = SwiGLU(xp @ [Wg; Wu]^T) per expert.
 cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, const int32_t* offsets,
                                __half* h, int* err, int rows_cap, int H, int E, int I, int max_ctas,
-                               cudaStream_t s)
+                               cudaStream_t s, int rows_hint)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, xp, (uint64_t)H, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
         !make_tmap(&tb, expert_weights, (uint64_t)H, (uint64_t)E * 3 * I))
         return cudaErrorInvalidValue;
-    cudaError_t e = set_gemm_attr<MODE_SWIGLU>();
-    if (e != cudaSuccess) return e;
     GemmArgs a = {};
     a.offsets = offsets;
     a.perm = nullptr;
@@ -505,23 +705,18 @@ cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, c
     a.b_nstep = 128;
     a.b_hi_delta = I;
     a.out_ld = I;
-    const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
-    e = launch_pdl(ffn_gemm_kernel<MODE_SWIGLU>, dim3(grid), dim3(GM_THREADS), gemm_smem_bytes(), s, ta, tb, a);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
+    return launch_ffn_any<MODE_SWIGLU>(ta, tb, a, rows_cap, rows_hint, max_ctas, true, s);
 }
 
 // GEMM2: expert_out[perm[r], :] = h[r, :] @ Wd^T per expert.
 cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
                              const int32_t* perm, __half* expert_out, int* err, int rows_cap, int H,
-                             int E, int I, int max_ctas, cudaStream_t s)
+                             int E, int I, int max_ctas, cudaStream_t s, int rows_hint)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
         !make_tmap(&tb, expert_weights, (uint64_t)I, (uint64_t)E * 3 * H))
         return cudaErrorInvalidValue;
-    cudaError_t e = set_gemm_attr<MODE_DOWN>();
-    if (e != cudaSuccess) return e;
     GemmArgs a = {};
     a.offsets = offsets;
     a.perm = perm;
@@ -536,10 +731,7 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
     a.b_nstep = GM_BN;
     a.b_hi_delta = 128;
     a.out_ld = H;
-    const int grid = grid_for(rows_cap, E, a.n_tiles, max_ctas);
-    e = launch_pdl(ffn_gemm_kernel<MODE_DOWN>, dim3(grid), dim3(GM_THREADS), gemm_smem_bytes(), s, ta, tb, a);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
+    return launch_ffn_any<MODE_DOWN>(ta, tb, a, rows_cap, rows_hint, max_ctas, true, s);
 }
 
 }  // namespace moe
@@ -551,14 +743,12 @@ namespace moe {
 cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, const int32_t* offsets,
                                  const unsigned long long* row_ptr, unsigned int* done_counter,
                                  unsigned long long* const* peer_flags, int npeers, int* err, int rows_cap,
-                                 int H, int E, int I, cudaStream_t s)
+                                 int H, int E, int I, cudaStream_t s, int rows_hint)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
         !make_tmap(&tb, expert_weights, (uint64_t)I, (uint64_t)E * 3 * H))
         return cudaErrorInvalidValue;
-    cudaError_t e = set_gemm_attr<MODE_DOWN_PTR>();
-    if (e != cudaSuccess) return e;
     GemmArgs a = {};
     a.offsets = offsets;
     a.err = err;
@@ -575,9 +765,7 @@ cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, 
     a.done_counter = done_counter;
     a.peer_flags = peer_flags;
     a.npeers = npeers;
-    const int grid = grid_for(rows_cap, E, a.n_tiles, 0);
-    ffn_gemm_kernel<MODE_DOWN_PTR><<<grid, GM_THREADS, gemm_smem_bytes(), s>>>(ta, tb, a);
-    return cudaGetLastError();
+    return launch_ffn_any<MODE_DOWN_PTR>(ta, tb, a, rows_cap, rows_hint, 0, false, s);
 }
 
 }  // namespace moe
