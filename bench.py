@@ -222,10 +222,17 @@ def run_ours(args):
     moe = __import__("_moe_loader").load()
     T, H, E, K, I, seed = moe.CONFIGS[args.config]
     dev = torch.device("cuda", local)
-    # every rank routes its own batch of T tokens (per-GPU work fixed as N grows);
-    # the weights are one model (same seed on every rank)
+    # weak scaling: every rank routes its own batch of T tokens (per-GPU work fixed
+    # as N grows); strong scaling: the config's one batch of T tokens is split into
+    # N slices of T/N.  The weights are one model (same seed on every rank).
     x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev, zipf=moe.inputs.ZIPF.get(args.config))
-    if rank > 0:
+    T_total = T
+    if args.scaling == "strong" and world > 1:
+        if T % world:
+            raise SystemExit(f"T={T} is not divisible by {world} GPUs")
+        T = T_total // world
+        x = x[rank * T:(rank + 1) * T].contiguous()
+    elif rank > 0:
         x = moe.make_inputs_torch(T, H, 1, 1, 8, seed + rank, device=dev)[0]
     y = torch.empty((T, H), dtype=torch.float16, device=dev)
     flush = torch.empty((L2_FLUSH_BYTES,), dtype=torch.uint8, device=dev)
@@ -345,6 +352,14 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, e2e_ms = float(t[0]), float(t[1])
+    # expert load over the whole job: (token, slot) rows per expert, summed over the
+    # ranks; with expert parallelism the busiest rank's rows set the step time
+    ids_chk, _ = moe.moe_routing_topk(x, wg, K)
+    counts = torch.bincount(ids_chk.flatten().long(), minlength=E)
+    counts_rank0 = counts.clone()
+    if world > 1:
+        dist.all_reduce(counts)
+    rank_rows = counts.view(world, E // world).sum(1).tolist() if world > 1 else [int(counts.sum())]
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -363,17 +378,19 @@ def run_ours(args):
         hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         comb_bytes = T * K * H * 2 + T * K * 2 + T * H * 2
         rout_bytes = T * H * 2 + H * E * 2 + T * K * 6
-        ids_chk, _ = moe.moe_routing_topk(x, wg, K)
-        load = torch.bincount(ids_chk.flatten().long(), minlength=E).float() / ids_chk.numel()
+        load = counts_rank0.float() / ids_chk.numel()
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I} per GPU",
-                       "global_batch": world * T, "parallelism": f"ep{world} (expert parallel, NCCL send/recv)" if world > 1 else "single GPU",
+            "config": {"workload": (f"{args.config} T={T} H={H} E={E} K={K} I={I} per GPU" if args.scaling == "weak" or world == 1
+                                    else f"{args.config} T={T_total} H={H} E={E} K={K} I={I} split over {world} GPUs ({T} per GPU)"),
+                       "global_batch": world * T, "parallelism": f"ep{world} (expert parallel, peer-memory row exchange over NVLink)" if world > 1 else "single GPU",
                        "l2": "flushed between timed steps (512 MB write)", "inputs": "seeded N(0,1)/N(0,1/fan_in) fp16" + (
                            ", w_gate columns scaled toward Zipf s=1 expert load" if args.config in moe.inputs.ZIPF else ""),
-                       "expert_load_rank0": [round(v, 4) for v in load.tolist()]},
+                       "expert_load_rank0": [round(v, 4) for v in load.tolist()],
+                       "rows_per_rank": rank_rows,
+                       "load_imbalance": max(rank_rows) / (sum(rank_rows) / len(rank_rows)) if sum(rank_rows) else None},
             "roofline": {"kernel": "gemm_swiglu (gate/up grouped GEMM + SwiGLU epilogue)", "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                          "peak_source": f"{peak_src} bf16_tflops (burst cuBLAS)",
@@ -414,6 +431,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-tokens", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="N>1: weak = T tokens per GPU (default); strong = the config's T split over the GPUs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
