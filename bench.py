@@ -196,19 +196,26 @@ def run_reference(args):
 
 # ============================================================================ our arm
 def cpu_baseline_sample(args, moe):
-    """The reference's CPU code on a bounded slice of the same workload (rank 0, N=1)."""
+    """The reference's CPU code on a bounded sample of the same workload (rank 0,
+    N=1): successive slices of the batch (wrapping at its end) until at least
+    --cpu-seconds of CPU time; tokens/s over the whole sample."""
     run, kind, (T, H, E, K, I), keep = cpu_reference_timer(args.config, moe)
     threads = os.cpu_count() or 1
-    sample = args.ref_tokens
+    chunk = max(1, min(args.ref_tokens, T))
     run(0, min(threads, T), threads)  # warm-up: page in the weights
-    s = time.perf_counter()
-    run(0, sample, threads)
-    dt = time.perf_counter() - s
+    tokens, spent, a = 0, 0.0, 0
+    while spent < args.cpu_seconds:
+        b = min(a + chunk, T)
+        s = time.perf_counter()
+        run(a, b, threads)
+        spent += time.perf_counter() - s
+        tokens += b - a
+        a = b % T
     if keep is not None:
         keep.close()
-    return {"value": sample / dt, "unit": "tokens/s", "cores": threads, "kind": kind,
-            "sample": f"first {sample} tokens of the {args.config} batch, NaiveMoE "
-                      f"(tests/moe_cpu_sim.cpp:183-306) over {threads} threads, {dt:.2f} s"}
+    return {"value": tokens / spent, "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{tokens} tokens of the {args.config} batch in slices of {chunk} from token 0, NaiveMoE "
+                      f"(tests/moe_cpu_sim.cpp:183-306) over {threads} threads, {spent:.1f} s"}
 
 
 def run_ours(args):
@@ -406,7 +413,10 @@ def run_ours(args):
                     "d2h_bytes_per_step": T * H * 2,
                     "how": "pinned host x -> device -> layer -> pinned host y every step; H2D and D2H on "
                            "two copy streams overlapping the neighbouring steps' compute"},
-            "gpu_launches": args.steps * (11 if world > 1 else 8),
+            # per step, one GPU: routing, fused permute, gather, gate/up GEMM, down GEMM,
+            # combine; expert parallel adds the count, plan, dispatch, row-pointer and two
+            # wait kernels and replaces gather + combine with the indexed combine
+            "gpu_launches": args.steps * (11 if world > 1 else 6),
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -429,7 +439,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="prefill")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-tokens", type=int, default=64)
+    ap.add_argument("--ref-tokens", type=int, default=256,
+                    help="tokens per CPU reference step (the reference arm) and per cpu_baseline slice")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU time the cpu_baseline sample runs for (whole slices, at least this long)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="N>1: weak = T tokens per GPU (default); strong = the config's T split over the GPUs")
