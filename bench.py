@@ -142,18 +142,49 @@ def reference_inputs(cfg, moe):
         (T, H, E, K, I)
 
 
-def cpu_reference_timer(cfg, moe):
-    """(timer object, kind): the reference's NaiveMoE (oracle/_ref) or, when that was
-    not built, the C restatement (oracle/_build)."""
-    from oracle import oracle as O
+class CpuReference:
+    """The reference's CPU layer on token slices: NaiveMoE (tests/moe_cpu_sim.cpp:183-306)
+    and TiledMoE (:543-569) from oracle/_ref, or, when that was not built, the C
+    restatement of NaiveMoE (oracle/_build; no tiled path)."""
 
-    (x, wg, ew), (T, H, E, K, I) = reference_inputs(cfg, moe)
-    if O.ref_available():
-        t = O.RefTimer(x, wg, ew, K)
-        return (lambda t0, t1, th: t.naive(t0, t1, th)), "reference", (T, H, E, K, I), t
-    def run(t0, t1, th):
-        return O.moe_naive(x[t0:t1], wg, ew, K, nthreads=th)[0]
-    return run, "port", (T, H, E, K, I), None
+    def __init__(self, cfg, moe):
+        from oracle import oracle as O
+
+        (self.x, self.wg, self.ew), self.shape = reference_inputs(cfg, moe)
+        self.O = O
+        self.kind = "reference" if O.ref_available() else "port"
+        self.t = O.RefTimer(self.x, self.wg, self.ew, self.shape[3]) if self.kind == "reference" else None
+
+    def run(self, path, t0, t1, threads):
+        if self.t is not None:
+            return (self.t.naive if path == "naive" else self.t.tiled)(t0, t1, threads)
+        if path != "naive":
+            raise RuntimeError("TiledMoE needs oracle/_ref")
+        return self.O.moe_naive(self.x[t0:t1], self.wg, self.ew, self.shape[3], nthreads=threads)[0]
+
+    def close(self):
+        if self.t is not None:
+            self.t.close()
+
+
+def cpu_slices(ref, path, chunk, threads, min_seconds=0.0, steps=None):
+    """Successive `chunk`-token slices of the batch from token 0 (wrapping), each run
+    over `threads` threads; either `steps` slices or whole slices until at least
+    min_seconds.  Returns (per-slice tokens/s list, tokens, seconds)."""
+    T = ref.shape[0]
+    chunk = max(1, min(chunk, T))
+    rates, tokens, spent, a, n = [], 0, 0.0, 0, 0
+    while (steps is not None and n < steps) or (steps is None and spent < min_seconds):
+        b = min(a + chunk, T)
+        s = time.perf_counter()
+        ref.run(path, a, b, threads)
+        dt = time.perf_counter() - s
+        rates.append((b - a) / dt)
+        spent += dt
+        tokens += b - a
+        a = b % T
+        n += 1
+    return rates, tokens, spent
 
 
 def run_reference(args):
@@ -161,61 +192,102 @@ def run_reference(args):
     if rank != 0:
         return 0
     moe = __import__("_moe_loader").load()
-    run, kind, (T, H, E, K, I), keep = cpu_reference_timer(args.config, moe)
+    ref = CpuReference(args.config, moe)
+    T, H, E, K, I = ref.shape
     threads = os.cpu_count() or 1
-    sample = args.ref_tokens
-    times = []
-    t0 = 0
-    for step in range(args.warmup + args.steps):
-        a = t0 % T
-        b = min(a + sample, T)
-        s = time.perf_counter()
-        run(a, b, threads)
-        dt = time.perf_counter() - s
-        if step >= args.warmup:
-            times.append((b - a) / dt)
-        t0 += sample
-    value = statistics.mean(times)
-    ms_per_step = 1000.0 * sample / value
+    sample = min(args.ref_tokens, T)
+    cpu_slices(ref, "naive", sample, threads, steps=args.warmup)  # pages the weights in
+    rates, tokens, spent = cpu_slices(ref, "naive", sample, threads, steps=args.steps)
+    value = tokens / spent
+    tiled = None
+    if ref.kind == "reference":
+        tr, ttok, tsp = cpu_slices(ref, "tiled", sample, threads, steps=max(1, args.steps // 4))
+        tiled = {"value": ttok / tsp, "unit": "tokens/s", "steps": len(tr),
+                 "sample": f"TiledMoE (tests/moe_cpu_sim.cpp:543-569) on {len(tr)} slices of {sample} tokens"}
+    ref.close()
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "ranks_used": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * spent / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.config} T={T} H={H} E={E} K={K} I={I}; each step = NaiveMoE on a "
-                               f"{sample}-token slice", "parallelism": "host threads"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
-                         "sample": f"{sample} tokens of the {args.config} batch per step, NaiveMoE "
-                                   f"(tests/moe_cpu_sim.cpp:183-306) split over {threads} threads"},
+                               f"{sample}-token slice of the batch (successive slices from token 0)",
+                   "parallelism": "host threads", "same_protocol_as": "the GPU arm's cpu_baseline"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": ref.kind,
+                         "sample": f"{tokens} tokens in slices of {sample} from token 0, NaiveMoE "
+                                   f"(tests/moe_cpu_sim.cpp:183-306) split over {threads} threads, {spent:.1f} s",
+                         "tiled": tiled},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    if keep is not None:
-        keep.close()
     return 0
 
 
 # ============================================================================ our arm
-def cpu_baseline_sample(args, moe):
+def cpu_baseline_sample(args, moe, ids_gpu=None):
     """The reference's CPU code on a bounded sample of the same workload (rank 0,
-    N=1): successive slices of the batch (wrapping at its end) until at least
-    --cpu-seconds of CPU time; tokens/s over the whole sample."""
-    run, kind, (T, H, E, K, I), keep = cpu_reference_timer(args.config, moe)
+    N=1): NaiveMoE on successive slices of the batch until at least --cpu-seconds,
+    then TiledMoE for a third of that; tokens/s over each whole sample.  Also the
+    near-tie census of the routing: the oracle's ids over the whole batch against the
+    GPU's (ids_gpu), tokens whose oracle top-(K+1) logit margin is < 1e-3 counted
+    apart (the reference's own tie order is unspecified, tests/moe_cpu_sim.cpp:232-233)."""
+    import numpy as np
+
+    ref = CpuReference(args.config, moe)
+    T, H, E, K, I = ref.shape
     threads = os.cpu_count() or 1
     chunk = max(1, min(args.ref_tokens, T))
-    run(0, min(threads, T), threads)  # warm-up: page in the weights
-    tokens, spent, a = 0, 0.0, 0
-    while spent < args.cpu_seconds:
-        b = min(a + chunk, T)
-        s = time.perf_counter()
-        run(a, b, threads)
-        spent += time.perf_counter() - s
-        tokens += b - a
-        a = b % T
-    if keep is not None:
-        keep.close()
-    return {"value": tokens / spent, "unit": "tokens/s", "cores": threads, "kind": kind,
-            "sample": f"{tokens} tokens of the {args.config} batch in slices of {chunk} from token 0, NaiveMoE "
-                      f"(tests/moe_cpu_sim.cpp:183-306) over {threads} threads, {spent:.1f} s"}
+    ref.run("naive", 0, min(threads, T), threads)  # warm-up: page in the weights
+    _, tokens, spent = cpu_slices(ref, "naive", chunk, threads, min_seconds=args.cpu_seconds)
+    out = {"value": tokens / spent, "unit": "tokens/s", "cores": threads, "kind": ref.kind,
+           "sample": f"{tokens} tokens of the {args.config} batch in slices of {chunk} from token 0, NaiveMoE "
+                     f"(tests/moe_cpu_sim.cpp:183-306) over {threads} threads, {spent:.1f} s"}
+    if ref.kind == "reference":
+        _, ttok, tsp = cpu_slices(ref, "tiled", chunk, threads, min_seconds=args.cpu_seconds / 3)
+        out["tiled"] = {"value": ttok / tsp, "unit": "tokens/s",
+                        "sample": f"{ttok} tokens in slices of {chunk}, TiledMoE (tests/moe_cpu_sim.cpp:543-569) "
+                                  f"over {threads} threads, {tsp:.1f} s"}
+    if ids_gpu is not None:
+        rid, _, _, _, margin = ref.O.routing(ref.x, ref.wg, K)
+        diff = np.any(ids_gpu != rid, axis=1)
+        near = margin < 1e-3
+        out["routing_parity"] = {"tokens": int(T), "near_ties": int(near.sum()),
+                                 "near_ties_differing": int((diff & near).sum()),
+                                 "differing_away_from_ties": int((diff & ~near).sum()),
+                                 "near_tie_rule": "oracle top-(K+1) logit margin < 1e-3"}
+    ref.close()
+    return out
+
+
+def _timed_steps(step, flush, stream, n, world):
+    """n steps, each after an L2 flush, bracketed by a barrier and a device sync on
+    both sides; -> per-step milliseconds (CUDA events on the launching stream)."""
+    import torch
+    import torch.distributed as dist
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(n):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return [s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)]
+
+
+def _max_over_ranks(vals, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
 
 
 def run_ours(args):
@@ -233,6 +305,7 @@ def run_ours(args):
     # as N grows); strong scaling: the config's one batch of T tokens is split into
     # N slices of T/N.  The weights are one model (same seed on every rank).
     x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev, zipf=moe.inputs.ZIPF.get(args.config))
+    x_cfg, ew_full = x, ew  # the config's batch and all experts (parity checks, strong record)
     T_total = T
     if args.scaling == "strong" and world > 1:
         if T % world:
@@ -247,24 +320,26 @@ def run_ours(args):
     ep = None
     if world > 1:
         # expert parallel: rank r keeps experts [r*E/N, (r+1)*E/N) and exchanges
-        # token rows with NCCL send/recv inside MoeEpLayerForward
+        # token rows with its peers inside MoeEpLayerForward
         if E % world:
             raise SystemExit(f"E={E} is not divisible by {world} GPUs")
         El = E // world
-        ew = ew[rank * El:(rank + 1) * El].contiguous()
-        torch.cuda.empty_cache()
+        ew = ew_full[rank * El:(rank + 1) * El].contiguous()
         uid = [moe.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ep = moe.EpContext(uid[0], rank, world, timeout_ms=120000)
         ws = torch.empty((ep.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
 
-        def step(xin=None):
-            ep.forward(x if xin is None else xin, wg, ew, K, y=y, workspace=ws)
+        def layer(xin, yout):
+            ep.forward(xin, wg, ew, K, y=yout, workspace=ws)
     else:
         ws = torch.empty((moe.moe_layer_workspace_size(T, H, E, K, I),), dtype=torch.uint8, device=dev)
 
-        def step(xin=None):
-            moe.moe_layer_forward(x if xin is None else xin, wg, ew, K, y=y, workspace=ws)
+        def layer(xin, yout):
+            moe.moe_layer_forward(xin, wg, ew, K, y=yout, workspace=ws)
+
+    def step():
+        layer(x, y)
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -273,39 +348,44 @@ def run_ours(args):
     if moe.device_error(ws) != 0:
         raise RuntimeError("device error during warm-up")
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        for i in range(args.steps):
-            flush.zero_()
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        step_ms = _timed_steps(step, flush, stream, args.steps, world)
+    total_ms = sum(step_ms)
     # stage times (and the roofline kernel's duration): a second pass of the same K
     # steps with CUDA events at the stage boundaries, kept out of the timed region so
     # the events do not stand between the kernels there
+    if world > 1:
+        dist.barrier()
     moe.trace_start(args.steps)
     for i in range(args.steps):
         flush.zero_()
         step()
     torch.cuda.synchronize()
     stages = moe.trace_stop(args.steps)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
     if moe.device_error(ws) != 0:
         raise RuntimeError("device error during the timed steps")
 
-    # End to end through the public API, as a serving loop would run it: every step
-    # copies its own x from pinned host memory and its y back to pinned host memory;
-    # the copies run on two copy streams (H2D, D2H) so that step i+1's input and
-    # step i-1's output cross PCIe while step i computes.  The timed region spans
-    # the first H2D to the last D2H (inputs > L2: the weights alone are 1.6 GB).
+    # ---- expert-parallel parity: rank r's y rows against the single-GPU layer with
+    # all experts on the same tokens (bit for bit: every kernel is the same)
+    ep_parity = None
+    if world > 1:
+        S = min(256, T)
+        y_one = moe.moe_layer_forward(x[:S].contiguous(), wg, ew_full, K)
+        torch.cuda.synchronize()
+        eq = torch.tensor([float(torch.equal(y_one, y[:S])), float((y_one.float() - y[:S].float()).abs().max())],
+                          dtype=torch.float64, device=dev)
+        allv = [torch.empty_like(eq) for _ in range(world)]
+        dist.all_gather(allv, eq)
+        ep_parity = {"tokens_per_rank": S, "ranks_bit_equal": int(sum(v[0].item() for v in allv)),
+                     "ranks": world, "max_abs_diff": max(v[1].item() for v in allv),
+                     "against": "MoeLayerForward on one GPU with all experts, same tokens"}
+
+    # ---- end to end through the public API, as a serving loop would run it: every
+    # step copies its own x from pinned host memory and its y back to pinned host
+    # memory; the copies run on two copy streams (H2D, D2H) so that step i+1's input
+    # and step i-1's output cross PCIe while step i computes.  The timed region spans
+    # the first H2D to the last D2H (inputs > L2: the weights alone are 1.6 GB).  All
+    # ranks start together (barrier), and the run lasts at least --e2e-seconds.
     x_host = [x.cpu().pin_memory(), x.cpu().pin_memory()]
     y_host = [torch.empty((T, H), dtype=torch.float16).pin_memory() for _ in range(2)]
     x_dev = [torch.empty_like(x), torch.empty_like(x)]
@@ -313,11 +393,14 @@ def run_ours(args):
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
 
-    def e2e_run(nsteps):
+    def e2e_run(nsteps, compute=True):
         in_ready = [ev(), ev()]
         x_free = [None, None]   # compute finished reading x_dev[b]
         y_free = [None, None]   # D2H finished reading y_dev[b]
         t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         t_start.record(h2d)
         with torch.cuda.stream(h2d):
             x_dev[0].copy_(x_host[0], non_blocking=True)
@@ -335,10 +418,8 @@ def run_ours(args):
             stream.wait_event(in_ready[b])
             if y_free[b] is not None:
                 stream.wait_event(y_free[b])
-            if ep is not None:
-                ep.forward(x_dev[b], wg, ew, K, y=y_dev[b], workspace=ws)
-            else:
-                moe.moe_layer_forward(x_dev[b], wg, ew, K, y=y_dev[b], workspace=ws)
+            if compute:
+                layer(x_dev[b], y_dev[b])
             done = ev()
             done.record(stream)
             x_free[b] = done
@@ -352,13 +433,50 @@ def run_ours(args):
         torch.cuda.synchronize()
         return t_start.elapsed_time(t_end)
 
+    mean_ms = total_ms / args.steps
+    e2e_steps = max(args.steps, int(args.e2e_seconds * 1000.0 / max(mean_ms, 1e-3)) + 1)
     e2e_run(args.warmup)
-    e2e_ms = e2e_run(args.steps)
+    e2e_ms = e2e_run(e2e_steps)
+    # the host-copy ceiling: the same copies on the same streams with no layer
+    copy_ms = e2e_run(e2e_steps, compute=False)
+    h2d_ms = _copy_only(x_host[0], x_dev[0], h2d, e2e_steps, world)
+    d2h_ms = _copy_only(y_dev[0], y_host[0], d2h, e2e_steps, world)
+    per_rank_copy = [h2d_ms, d2h_ms]
 
-    t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    # ---- sustained: back-to-back layer steps for --sustained-seconds (the serving
+    # case under the power cap), clocks sampled over them; then a traced pass of 20
+    # steps while the GPU is still hot, for GEMM1's rate at those clocks
+    sus_steps = int(args.sustained_seconds * 1000.0 / max(mean_ms, 1e-3)) + 1 if args.sustained_seconds > 0 else 0
+    sus = None
+    if sus_steps:
+        with ClockSampler(local) as clk_sus:
+            sus_ms = _timed_steps(step, flush, stream, sus_steps, world)
+            moe.trace_start(20)
+            for _ in range(20):
+                flush.zero_()
+                step()
+            torch.cuda.synchronize()
+            sus_stages = moe.trace_stop(20)
+        sus = {"steps": sus_steps, "ms_total": sum(sus_ms), "clk": clk_sus.summary(),
+               "g1_ms": statistics.mean(c["gemm_swiglu"] for c in sus_stages)}
+
+    # ---- strong scaling record (N>1): the config's one batch of T tokens split over
+    # the N ranks, same process; efficiency against rank 0's single-GPU layer on the
+    # whole batch with all experts
+    strong = None
+    if world > 1 and args.scaling == "weak" and not args.no_strong:
+        strong = _strong_record(args, moe, x_cfg, wg, ew_full, ew, ep, K, H, E, I, T_total, flush, stream,
+                                rank, world, dev)
+
+    r = _max_over_ranks([total_ms, e2e_ms, copy_ms, h2d_ms, d2h_ms] + ([sus["ms_total"]] if sus else []), world, dev)
+    total_ms, e2e_ms, copy_ms = r[0], r[1], r[2]
+    if sus:
+        sus["ms_total"] = r[5]
+    copies = [torch.zeros(2, dtype=torch.float64, device=dev) for _ in range(world)]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms = float(t[0]), float(t[1])
+        dist.all_gather(copies, torch.tensor(per_rank_copy, dtype=torch.float64, device=dev))
+    else:
+        copies = [torch.tensor(per_rank_copy, dtype=torch.float64)]
     # expert load over the whole job: (token, slot) rows per expert, summed over the
     # ranks; with expert parallelism the busiest rank's rows set the step time
     ids_chk, _ = moe.moe_routing_topk(x, wg, K)
@@ -372,10 +490,12 @@ def run_ours(args):
         peaks, peak_src = load_peaks()
         ms = total_ms / args.steps
         value = world * T * args.steps / (total_ms / 1e3)
-        e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+        e2e_value = world * T * e2e_steps / (e2e_ms / 1e3)
         stage_avg = {k: statistics.mean(c[k] for c in stages) for k in moe.TRACE_STAGES}
-        g1_flops = 2.0 * T * K * H * 2 * I
-        g2_flops = 2.0 * T * K * I * H
+        # GEMM FLOPs on the rows this rank's experts received (weak: ~T*K per rank)
+        rows0 = rank_rows[0] if world > 1 else T * K
+        g1_flops = 2.0 * rows0 * H * 2 * I
+        g2_flops = 2.0 * rows0 * I * H
         g1_ms = stage_avg["gemm_swiglu"]
         ach = g1_flops / (g1_ms / 1e3) / 1e12
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -387,6 +507,7 @@ def run_ours(args):
         comb_bytes = T * K * H * 2 + T * K * 2 + T * H * 2
         rout_bytes = T * H * 2 + H * E * 2 + T * K * 6
         load = counts_rank0.float() / ids_chk.numel()
+        xbytes = T * H * 2
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -404,6 +525,7 @@ def run_ours(args):
                        "load_imbalance": max(rank_rows) / (sum(rank_rows) / len(rank_rows)) if sum(rank_rows) else None},
             "roofline": {"kernel": "gemm_swiglu (gate/up grouped GEMM + SwiGLU epilogue)", "bound": "tensor",
                          "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                         "rows": rows0,
                          "peak_source": f"{peak_src} bf16_tflops (burst cuBLAS)",
                          # the kernel runs inside back-to-back layer steps under the power cap, so
                          # the sustained cuBLAS figure is the other fair denominator
@@ -412,23 +534,41 @@ def run_ours(args):
             "ffn": {"tflops": ffn_tf, "frac_of_peak": ffn_tf / peak, "ms": ffn_ms,
                     "frac_of_datasheet_2250": ffn_tf / 2250.0},
             "stages_ms": stage_avg,
-            "stages_how": "CUDA events at stage boundaries, a second pass of the same steps",
+            "stages_how": "CUDA events at stage boundaries, a second pass of the same steps (rank 0)",
             "hbm_kernels": {"combine_gbs": comb_bytes / (stage_avg["combine"] / 1e3) / 1e9 if stage_avg["combine"] else None,
                             "routing_gbs": rout_bytes / (stage_avg["routing"] / 1e3) / 1e9 if stage_avg["routing"] else None,
                             "hbm_peak_gbs": hbm},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": xbytes,
+                    "d2h_bytes_per_step": xbytes, "steps": e2e_steps, "ms": e2e_ms,
                     "how": "pinned host x -> device -> layer -> pinned host y every step; H2D and D2H on "
-                           "two copy streams overlapping the neighbouring steps' compute"},
+                           "two copy streams overlapping the neighbouring steps' compute; ranks start "
+                           "together (barrier); max over ranks",
+                    "copy_only_ceiling": world * T * e2e_steps / (copy_ms / 1e3),
+                    "per_rank_copy_gbs": [{"h2d": xbytes * e2e_steps / (c[0].item() / 1e3) / 1e9,
+                                           "d2h": xbytes * e2e_steps / (c[1].item() / 1e3) / 1e9} for c in copies]},
             # per step, one GPU: routing, fused permute, gather, gate/up GEMM, down GEMM,
-            # combine; expert parallel adds the count, plan, dispatch, row-pointer and two
-            # wait kernels and replaces gather + combine with the indexed combine
+            # combine; expert parallel: routing, permute, counts, plan, dispatch,
+            # row-pointer, rows wait, gate/up GEMM, down GEMM, return wait, combine
             "gpu_launches": args.steps * (11 if world > 1 else 6),
             "clocks": clk.summary(),
         }
+        if ep_parity is not None:
+            line["ep_parity"] = ep_parity
+        if sus:
+            sv = world * T * sus["steps"] / (sus["ms_total"] / 1e3)
+            g1s = g1_flops / (sus["g1_ms"] / 1e3) / 1e12
+            line["sustained"] = {"value": sv, "unit": "tokens/s", "steps": sus["steps"],
+                                 "seconds": sus["ms_total"] / 1e3, "clocks": sus["clk"],
+                                 "gemm_swiglu_tflops": g1s,
+                                 "gemm_swiglu_frac_of_sustained": g1s / peak_sus if peak_sus else None,
+                                 "gemm_swiglu_frac_of_burst": g1s / peak,
+                                 "how": "back-to-back layer steps (L2 flush between), device time, max over "
+                                        "ranks; GEMM1 from a traced pass of 20 steps right after"}
+        if strong is not None:
+            line["strong"] = strong
         if world == 1 and not args.no_cpu_baseline:
             try:
-                line["cpu_baseline"] = cpu_baseline_sample(args, moe)
+                line["cpu_baseline"] = cpu_baseline_sample(args, moe, ids_gpu=ids_chk.cpu().numpy())
             except Exception as exc:  # reported, never fatal for the GPU number
                 line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
         print(json.dumps(line), flush=True)
@@ -437,6 +577,93 @@ def run_ours(args):
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def _copy_only(src, dst, s, n, world):
+    """n back-to-back copies src -> dst on stream s, all ranks at once -> ms."""
+    import torch
+    import torch.distributed as dist
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(n):
+            dst.copy_(src, non_blocking=True)
+    b.record(s)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def _strong_record(args, moe, x_cfg, wg, ew_full, ew_local, ep, K, H, E, I, T_total, flush, stream, rank,
+                   world, dev):
+    """The config's batch of T_total tokens split into N slices of T_total/N, one per
+    rank, through the same expert-parallel context; y checked bit for bit against the
+    single-GPU layer on the same tokens; efficiency against rank 0's single-GPU
+    layer on the whole batch."""
+    import torch
+    import torch.distributed as dist
+
+    if T_total % world:
+        return {"skipped": f"T={T_total} not divisible by {world}"}
+    Tl = T_total // world
+    xs = x_cfg[rank * Tl:(rank + 1) * Tl].contiguous()
+    ys = torch.empty((Tl, H), dtype=torch.float16, device=dev)
+    ws = torch.empty((ep.workspace_size(Tl, H, E, K, I),), dtype=torch.uint8, device=dev)
+
+    def st():
+        ep.forward(xs, wg, ew_local, K, y=ys, workspace=ws)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        st()
+    torch.cuda.synchronize()
+    ms = _timed_steps(st, flush, stream, args.steps, world)
+    dist.barrier()
+    moe.trace_start(args.steps)
+    for _ in range(args.steps):
+        flush.zero_()
+        st()
+    torch.cuda.synchronize()
+    stages = moe.trace_stop(args.steps)
+    err = moe.device_error(ws)
+    y_one = moe.moe_layer_forward(xs, wg, ew_full, K)
+    torch.cuda.synchronize()
+    eq = float(torch.equal(y_one, ys))
+    ids, _ = moe.moe_routing_topk(xs, wg, K)
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    dist.all_reduce(counts)
+    rank_rows = counts.view(world, E // world).sum(1).tolist()
+    # single-GPU reference run on rank 0 (the others wait at the barrier)
+    single_ms = 0.0
+    if rank == 0:
+        y1 = torch.empty((T_total, H), dtype=torch.float16, device=dev)
+        ws1 = torch.empty((moe.moe_layer_workspace_size(T_total, H, E, K, I),), dtype=torch.uint8, device=dev)
+
+        def one():
+            moe.moe_layer_forward(x_cfg, wg, ew_full, K, y=y1, workspace=ws1)
+
+        for _ in range(args.warmup):
+            flush.zero_()
+            one()
+        single_ms = sum(_timed_steps(one, flush, stream, args.steps, 1))
+        del y1, ws1
+    dist.barrier()
+    t = torch.tensor([sum(ms), float(err != 0), 1.0 - eq], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, any_err, any_diff = t.tolist()
+    value = T_total * args.steps / (total_ms / 1e3)
+    single = T_total * args.steps / (single_ms / 1e3) if single_ms else None
+    return {"value": value, "unit": "tokens/s", "T_total": T_total, "tokens_per_rank": Tl,
+            "ms_per_step": total_ms / args.steps, "single_gpu_value": single,
+            "efficiency": value / (world * single) if single else None,
+            "rows_per_rank": rank_rows, "load_imbalance": max(rank_rows) / (sum(rank_rows) / world),
+            "stages_ms_rank0": {k: statistics.mean(c[k] for c in stages) for k in moe.TRACE_STAGES},
+            "ranks_bit_equal_to_single_gpu": not any_diff, "device_error": bool(any_err),
+            "how": "same process after the weak record; device time, max over ranks; single-GPU value: rank 0, "
+                   "MoeLayerForward on the whole batch with all experts"}
 
 
 def main():
@@ -451,6 +678,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU time the cpu_baseline sample runs for (whole slices, at least this long)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-seconds", type=float, default=1.0, help="minimum length of the timed e2e run")
+    ap.add_argument("--sustained-seconds", type=float, default=3.0,
+                    help="length of the sustained record (back-to-back steps); 0 skips it")
+    ap.add_argument("--no-strong", action="store_true", help="N>1: skip the strong-scaling record")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="N>1: weak = T tokens per GPU (default); strong = the config's T split over the GPUs")
     args = ap.parse_args()

@@ -369,43 +369,6 @@ __global__ void ep_p2p_wait_kernel(const unsigned long long* flag, unsigned long
     if (threadIdx.x == 0) ep_wait_flag(flag, target, err, code);
 }
 
-// combine over the returned rows, after every expert owner has signalled them
-__global__ void __launch_bounds__(256)
-ep_p2p_combine_kernel(const __half* __restrict__ ret, const int32_t* __restrict__ dest,
-                      const __half* __restrict__ weights, __half* __restrict__ y, int T, int H, int K,
-                      const unsigned long long* flag, unsigned long long target, int* err)
-{
-    // on timeout the rows are stale; the error word says so
-    if (threadIdx.x == 0) ep_wait_flag(flag, target, err, EP_ERR_WAIT_RET);
-    __syncthreads();
-    const int vpr = H >> 3;
-    const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (v >= (long long)T * vpr) return;
-    const int t = (int)(v / vpr);
-    const int c = (int)(v - (long long)t * vpr) << 3;
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = 0.0f;
-    for (int k = 0; k < K; k++) {
-        const float w = __half2float(weights[(size_t)t * K + k]);
-        const int r = dest[(size_t)t * K + k];
-        uint4 q = __ldcv(reinterpret_cast<const uint4*>(ret + (size_t)r * H + c));  // written by peers
-        const __half2* q2 = reinterpret_cast<const __half2*>(&q);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float2 f = __half22float2(q2[i]);
-            acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
-            acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
-        }
-    }
-    uint4 o;
-    o.x = moe::pack_half2(acc[0], acc[1]);
-    o.y = moe::pack_half2(acc[2], acc[3]);
-    o.z = moe::pack_half2(acc[4], acc[5]);
-    o.w = moe::pack_half2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
-}
-
 }  // namespace
 
 namespace {
@@ -603,7 +566,8 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
     }
     moe::trace_mark(ev, 1, s);
     if ((e = moe::launch_permute(ids, TK, (int)E, at<int32_t>(ws, L.chunk_counts),
-                                 at<int32_t>(ws, L.chunk_base), offsets, perm, dest, err, s)) != cudaSuccess)
+                                 at<int32_t>(ws, L.chunk_base), offsets, perm, dest, err, moe::routing_error_word(),
+                                 s)) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
     if (T > 0 && (e = moe::launch_gather_rows(static_cast<const __half*>(x), perm, offsets, (int)E, (int)K,
@@ -862,7 +826,7 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 1, s);
     if (moe::launch_permute(ids, TK, (int)E, at<int32_t>(ws, L.chunk_counts), at<int32_t>(ws, L.chunk_base),
-                            offsets, perm, dest, err, s) != cudaSuccess)
+                            offsets, perm, dest, err, moe::routing_error_word(), s) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
     ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n);
@@ -891,13 +855,12 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 5, s);
-    const long long nv = (long long)T * (H >> 3);
-    if (nv > 0) {
-        ep_p2p_combine_kernel<<<(int)((nv + 255) / 256), 256, 0, s>>>(ret_local, dest, wts, static_cast<__half*>(y),
-                                                                     (int)T, (int)H, (int)K, flags + 2, target, err);
-    } else {
-        ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 2, target, err, EP_ERR_WAIT_RET);
-    }
+    // one bounded wait for every owner's returned rows, then the combine through the
+    // inverse permutation (a timed-out wait leaves stale rows; the error word says so)
+    ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 2, target, err, EP_ERR_WAIT_RET);
+    if (T > 0 && moe::launch_combine_indexed(ret_local, dest, wts, static_cast<__half*>(y), (int)T, (int)H, (int)K,
+                                             s) != cudaSuccess)
+        return MOE_ERR_CUDA;
     if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 6, s);
     return MOE_OK;

@@ -34,7 +34,13 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
 
 cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
                            int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,
-                           int* err, cudaStream_t s);
+                           int* err, int* fold, cudaStream_t s);
+
+// Device address of the routing kernel's error word on the current device (the
+// word its bounded waits record into; MoeRoutingTopK has no workspace).  Layer
+// calls pass it to launch_permute as `fold`, which moves it into the call's error
+// word.  nullptr if the lookup fails.
+int* routing_error_word();
 
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* offsets, int E,
                                int K, int H, int rows_cap, __half* xp, cudaStream_t s);

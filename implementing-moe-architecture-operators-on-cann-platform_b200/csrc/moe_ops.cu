@@ -145,22 +145,23 @@ T* at(void* base, size_t off)
     return reinterpret_cast<T*>(static_cast<uint8_t*>(base) + off);
 }
 
+// fold: the routing error word when a routing launch precedes (layer calls), else nullptr
 int run_permute(const int32_t* ids, int64_t T, int64_t K, int64_t E, void* ws, const PermLayout& L,
-                int32_t* perm, int32_t* offsets, cudaStream_t s)
+                int32_t* perm, int32_t* offsets, cudaStream_t s, int* fold = nullptr)
 {
-    int* err = at<int>(ws, L.err);  // cleared by the permutation launch
+    int* err = at<int>(ws, L.err);  // cleared (or set to the folded routing error) by the permutation launch
     cudaError_t e = moe::launch_permute(ids, (int)(T * K), (int)E, at<int32_t>(ws, L.chunk_counts),
-                            at<int32_t>(ws, L.chunk_base), offsets, perm, nullptr, err, s);
+                            at<int32_t>(ws, L.chunk_base), offsets, perm, nullptr, err, fold, s);
     return cuda_status(e);
 }
 
 int run_ffn(const void* x, const int32_t* ids, const void* ew, void* out, int64_t T, int64_t H,
             int64_t E, int64_t K, int64_t I, void* ws, const FfnLayout& L, cudaStream_t s,
-            cudaEvent_t* ev)
+            cudaEvent_t* ev, int* fold = nullptr)
 {
     int32_t* perm = at<int32_t>(ws, L.p.perm);
     int32_t* offsets = at<int32_t>(ws, L.p.offsets);
-    int rc = run_permute(ids, T, K, E, ws, L.p, perm, offsets, s);
+    int rc = run_permute(ids, T, K, E, ws, L.p, perm, offsets, s, fold);
     if (rc != MOE_OK) return rc;
     trace_mark(ev, 2, s);
     if (T == 0) return MOE_OK;
@@ -279,7 +280,9 @@ int MoeLayerForward(const void* x, const void* w_gate, const void* expert_weight
                                              (int)K, s));
     if (rc != MOE_OK) return rc;
     trace_mark(ev, 1, s);
-    rc = run_ffn(x, expert_ids, expert_weights, expert_out, T, H, E, K, I, workspace, L.f, s, ev);
+    // the permutation moves a routing wait timeout into this call's error word
+    rc = run_ffn(x, expert_ids, expert_weights, expert_out, T, H, E, K, I, workspace, L.f, s, ev,
+                 moe::routing_error_word());
     if (rc != MOE_OK) return rc;
     rc = cuda_status(moe::launch_combine(static_cast<const __half*>(expert_out),
                                          static_cast<const __half*>(weights),
@@ -311,6 +314,21 @@ int MoeGetDeviceError(const void* workspace, int* code, void* stream)
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int v = 0;
     cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    *code = v;
+    return MOE_OK;
+}
+
+int MoeRoutingGetDeviceError(int* code, void* stream)
+{
+    if (!code) return MOE_ERR_NULL_POINTER;
+    int* word = moe::routing_error_word();
+    if (!word) return cuda_status(cudaErrorInvalidSymbol);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(word, 0, sizeof(int), s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_status(e);
     *code = v;

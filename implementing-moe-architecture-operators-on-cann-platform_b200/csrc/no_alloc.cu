@@ -21,6 +21,14 @@
 // call and overwrites everything else before reading it.  Calls that overlap on
 // the GPU (on different streams, or from several host threads) race on the
 // array and must be serialised by the caller.
+//
+// Device-side failures (an expert id outside [0,E), a bounded wait that gave up)
+// land in the error word at the start of the array, as they land in word 0 of a
+// caller's workspace on the ordinary path; MoeNoAllocGetDeviceError reads it.
+//
+// The cached address belongs to the device's primary context: do not keep using
+// the entry point across cudaDeviceReset (the module is reloaded and the array
+// may move).
 #include <mutex>
 
 #include "../../include/moe_ops.h"
@@ -66,4 +74,13 @@ extern "C" int MoeExpertFFNNoAlloc(const void* x, const int32_t* expert_ids, con
     if (rc != MOE_OK) return rc;
     return MoeExpertFFN(x, expert_ids, weights, expert_weights, expert_out, T, H, E, K, I, scratch,
                         (size_t)MOE_NO_ALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int MoeNoAllocGetDeviceError(int* code, void* stream)
+{
+    if (!code) return MOE_ERR_NULL_POINTER;
+    void* scratch = nullptr;
+    int rc = scratch_address(&scratch);
+    if (rc != MOE_OK) return rc;
+    return MoeGetDeviceError(scratch, code, stream);
 }

@@ -138,7 +138,7 @@ gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ per
 __global__ void __launch_bounds__(PC)
 perm_fused_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ chunk_counts,
                   int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int32_t* __restrict__ dest,
-                  int* __restrict__ err)
+                  int* __restrict__ err, int* __restrict__ fold)
 {
     extern __shared__ int pf_smem[];
     int* hist = pf_smem;          // [E]
@@ -150,7 +150,9 @@ perm_fused_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __rest
     const int nchunks = gridDim.x;
     if (threadIdx.x == 0) {
         bad = 0;
-        if (blockIdx.x == 0) *err = 0;  // this call's error word starts clear (set only after the sync)
+        // this call's error word starts clear (set only after the sync), or with the
+        // error the routing launch before it left in `fold` (which is cleared)
+        if (blockIdx.x == 0) *err = fold ? atomicExch(fold, 0) : 0;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int idx = blockIdx.x * PC + threadIdx.x;
@@ -232,6 +234,12 @@ copy_rows_kernel(const __half* __restrict__ src, const int32_t* __restrict__ idx
     for (int v = lane; v < nv; v += 32) d4[v] = __ldg(s4 + v);
 }
 
+// Error word of a call: cleared, or set to the routing error `fold` held (then cleared).
+__global__ void err_init_kernel(int* err, int* fold)
+{
+    *err = fold ? atomicExch(fold, 0) : 0;
+}
+
 cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, int H, __half* dst,
                              cudaStream_t s)
 {
@@ -242,7 +250,7 @@ cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, in
 
 cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
                            int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,
-                           int* err, cudaStream_t s)
+                           int* err, int* fold, cudaStream_t s)
 {
     const int nchunks = (n + PC - 1) / PC;
     // one cooperative launch when every chunk's block can be resident at once
@@ -258,14 +266,13 @@ cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_coun
     }
     if (nchunks > 0 && dev >= 0 && dev < 64 && nchunks <= capacity[dev]) {
         void* args[] = {(void*)&ids, (void*)&n, (void*)&E, (void*)&chunk_counts, (void*)&offsets,
-                        (void*)&perm, (void*)&dest, (void*)&err};
+                        (void*)&perm, (void*)&dest, (void*)&err, (void*)&fold};
         cudaError_t e = cudaLaunchCooperativeKernel((const void*)perm_fused_kernel, dim3(nchunks), dim3(PC), args,
                                                     fsmem, s);
         if (e == cudaSuccess) return cudaSuccess;
         cudaGetLastError();  // fall back to the three-kernel path
     }
-    cudaError_t me = cudaMemsetAsync(err, 0, sizeof(int), s);
-    if (me != cudaSuccess) return me;
+    err_init_kernel<<<1, 1, 0, s>>>(err, fold);
     if (nchunks > 0) {
         perm_count_kernel<<<nchunks, PC, E * sizeof(int), s>>>(ids, n, E, chunk_counts, err);
     }

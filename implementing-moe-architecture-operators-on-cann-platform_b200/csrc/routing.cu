@@ -438,6 +438,22 @@ typedef CUresult (*RtEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+int* routing_error_word()
+{
+    static int* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_routing_err) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        addr[dev] = static_cast<int*>(p);
+    }
+    return addr[dev];
+}
+
 cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights, int T, int H,
                            int E, int K, cudaStream_t s)
 {

@@ -100,6 +100,12 @@ int MoeExpertFFNNoAlloc(const void* x, const int32_t* expert_ids, const void* we
                         int64_t hiddenSize, int64_t numExperts, int64_t topK,
                         int64_t intermediateSize, void* stream);
 
+/* The device error word of MoeExpertFFNNoAlloc (it has no caller workspace for
+ * MoeGetDeviceError to read): synchronises `stream` and writes the code the last
+ * call recorded (same codes as MoeGetDeviceError) into *code.  Each call of the
+ * entry point starts with the word cleared.  No counterpart in the reference. */
+int MoeNoAllocGetDeviceError(int* code, void* stream);
+
 /* ------------------------------------------------------------------ whole layer */
 
 /* The three operators in sequence (the flow of tests/test_moe.cpp:446-463), with
@@ -177,6 +183,14 @@ int MoePermute(const int32_t* expert_ids, int32_t* perm, int32_t* expert_offsets
                size_t workspaceBytes, void* stream);
 
 /* ------------------------------------------------------------------ diagnostics */
+
+/* MoeRoutingTopK has no workspace: a bounded wait inside the routing kernel that
+ * gave up (never expected; 4/8 = a tensor-core or epilogue wait) is recorded in a
+ * per-device word of the library.  This synchronises `stream`, writes that word to
+ * *code and clears it.  Layer calls (MoeLayerForward, MoeEpLayerForward) move the
+ * word into their own error word instead.  Concurrent routing calls on one device
+ * share the word.  No counterpart in the reference (its kernels return void). */
+int MoeRoutingGetDeviceError(int* code, void* stream);
 
 /* Synchronises `stream` and reads the device error word of a MoeExpertFFN,
  * MoeLayerForward, MoePermute or MoeEpLayerForward workspace into *code (0 = none;

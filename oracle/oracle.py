@@ -26,8 +26,9 @@ _i32p = ctypes.POINTER(ctypes.c_int32)
 _c_int = ctypes.c_int
 
 
-def build(ref_dir: str | None = "/root/reference") -> None:
-    """Compile the restatement, and the reference itself when its sources exist."""
+def build(ref_dir: str | None = None) -> None:
+    """Compile the restatement, and the reference itself when its sources exist
+    (ref_dir: the reference checkout; None builds the restatement only)."""
     subprocess.check_call(["make", "-s", "-C", HERE, "oracle"])
     if ref_dir and os.path.isfile(os.path.join(ref_dir, "tests", "moe_cpu_sim.cpp")):
         subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={ref_dir}"])
@@ -84,6 +85,7 @@ def ref():
         R.ref_ctx_create.restype = ctypes.c_void_p
         R.ref_ctx_destroy.argtypes = [ctypes.c_void_p]
         R.ref_ctx_naive.argtypes = [ctypes.c_void_p, _c_int, _c_int, _c_int, _f32p]
+        R.ref_ctx_tiled.argtypes = [ctypes.c_void_p, _c_int, _c_int, _c_int, _f32p]
         _ref = R
     return _ref
 
@@ -233,6 +235,12 @@ class RefTimer:
     def naive(self, t0, t1, nthreads):
         y = np.empty((t1 - t0, self.H), np.float32)
         ref().ref_ctx_naive(self.h, t0, t1, nthreads, y.ctypes.data_as(_f32p))
+        return y
+
+    def tiled(self, t0, t1, nthreads):
+        """TiledMoE (tests/moe_cpu_sim.cpp:543-569) on tokens [t0, t1)."""
+        y = np.empty((t1 - t0, self.H), np.float32)
+        ref().ref_ctx_tiled(self.h, t0, t1, nthreads, y.ctypes.data_as(_f32p))
         return y
 
     def close(self):

@@ -24,6 +24,32 @@ struct RefCtx {
 std::vector<float> vec(const float* p, size_t n) { return std::vector<float>(p, p + n); }
 }  // namespace
 
+namespace {
+// Runs `path` (NaiveMoE or TiledMoE) over tokens [t0, t1), split into nthreads
+// contiguous token ranges on nthreads threads; y receives (t1-t0) rows.
+template <class Path>
+void ctx_run(RefCtx* c, int t0, int t1, int nthreads, float* y, Path path)
+{
+    int n = t1 - t0;
+    if (n <= 0) return;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > n) nthreads = n;
+    auto work = [&](int a, int b) {
+        std::vector<float> xs(c->x.begin() + (size_t)a * c->H, c->x.begin() + (size_t)b * c->H);
+        std::vector<float> out;
+        path(xs, c->w_gate, c->ew, b - a, c->H, c->E, c->K, c->I, out);
+        std::copy(out.begin(), out.end(), y + (size_t)(a - t0) * c->H);
+    };
+    std::vector<std::thread> th;
+    for (int i = 0; i < nthreads; i++) {
+        int a = t0 + (int)((long long)n * i / nthreads);
+        int b = t0 + (int)((long long)n * (i + 1) / nthreads);
+        th.emplace_back(work, a, b);
+    }
+    for (auto& t : th) t.join();
+}
+}  // namespace
+
 extern "C" {
 
 void ref_naive_moe(const float* x, const float* wg, const float* ew, int T, int H, int E, int K,
@@ -91,28 +117,21 @@ void* ref_ctx_create(const float* x, const float* wg, const float* ew, int T, in
 
 void ref_ctx_destroy(void* h) { delete static_cast<RefCtx*>(h); }
 
+// TiledMoE (tests/moe_cpu_sim.cpp:543-569) over tokens [t0, t1) on nthreads threads.
+void ref_ctx_tiled(void* h, int t0, int t1, int nthreads, float* y)
+{
+    ctx_run(static_cast<RefCtx*>(h), t0, t1, nthreads, y,
+            [](const std::vector<float>& x, const std::vector<float>& wg, const std::vector<float>& ew, int T,
+               int H, int E, int K, int I, std::vector<float>& out) { TiledMoE(x, wg, ew, T, H, E, K, I, out); });
+}
+
 // NaiveMoE over tokens [t0, t1), split over nthreads threads; y receives
 // (t1-t0) rows.  Which is what tests/moe_cpu_sim.cpp computes for those rows.
 void ref_ctx_naive(void* h, int t0, int t1, int nthreads, float* y)
 {
-    RefCtx* c = static_cast<RefCtx*>(h);
-    int n = t1 - t0;
-    if (n <= 0) return;
-    if (nthreads < 1) nthreads = 1;
-    if (nthreads > n) nthreads = n;
-    auto work = [&](int a, int b) {
-        std::vector<float> xs(c->x.begin() + (size_t)a * c->H, c->x.begin() + (size_t)b * c->H);
-        std::vector<float> out;
-        NaiveMoE(xs, c->w_gate, c->ew, b - a, c->H, c->E, c->K, c->I, out);
-        std::copy(out.begin(), out.end(), y + (size_t)(a - t0) * c->H);
-    };
-    std::vector<std::thread> th;
-    for (int i = 0; i < nthreads; i++) {
-        int a = t0 + (int)((long long)n * i / nthreads);
-        int b = t0 + (int)((long long)n * (i + 1) / nthreads);
-        th.emplace_back(work, a, b);
-    }
-    for (auto& t : th) t.join();
+    ctx_run(static_cast<RefCtx*>(h), t0, t1, nthreads, y,
+            [](const std::vector<float>& x, const std::vector<float>& wg, const std::vector<float>& ew, int T,
+               int H, int E, int K, int I, std::vector<float>& out) { NaiveMoE(x, wg, ew, T, H, E, K, I, out); });
 }
 
 }  // extern "C"

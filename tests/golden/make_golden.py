@@ -10,7 +10,8 @@ Small cases store their inputs; larger ones store only a SHA-256 of the inputs
 make_inputs() regenerates, so a generator change is detected instead of silently
 comparing different data.
 
-    python tests/golden/make_golden.py      # needs the reference sources
+    python tests/golden/make_golden.py [REFERENCE_CHECKOUT]   # needs the reference sources
+    (default: MOE_REFERENCE_DIR, else a "reference" directory beside the repository)
 """
 import hashlib
 import os
@@ -43,7 +44,9 @@ def input_digest(x, wg, ew):
 
 
 def main():
-    O.build()
+    ref = (sys.argv[1] if len(sys.argv) > 1 else None) or os.environ.get("MOE_REFERENCE_DIR") or \
+        os.path.join(os.path.dirname(ROOT), "reference")
+    O.build(ref)
     make_inputs = load().make_inputs
     for name, (T, H, E, K, I, seed, store) in CASES.items():
         x, wg, ew = make_inputs(T, H, E, K, I, seed)

@@ -84,7 +84,22 @@ def _free_port():
     return p
 
 
-def _ep_rank(rank, n, port, shape, path, q):
+# Multi-GPU cases: every (shape, path) runs in the same n spawned ranks.  E is a
+# multiple of 8 so every case runs at 2, 4 and 8 ranks; (384, 512, 64, 6, 256) is the
+# fine-grained top-6 layer, (1024, 2048, 16, 2, 1024) has the headline H/E/K.
+MULTI_SHAPES = [(300, 256, 8, 2, 512), (1024, 2048, 16, 2, 1024), (384, 512, 64, 6, 256)]
+Y_TOKENS = 128  # y rows per rank checked against the oracle
+
+
+def _ep_inputs(moe, shape, rank):
+    """numpy fp16: this rank's tokens (seed 1000+rank) and the one model (seed 7)."""
+    T, H, E, K, I = shape
+    x = moe.make_inputs(T, H, 1, 1, 8, 1000 + rank)[0]
+    _, wg, ew = moe.make_inputs(T, H, E, K, I, 7)
+    return x, wg, ew
+
+
+def _ep_rank(rank, n, port, q):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -93,55 +108,85 @@ def _ep_rank(rank, n, port, shape, path, q):
     from _moe_loader import load
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    if path == "nccl":
-        os.environ["MOE_EP_FORCE_NCCL"] = "1"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=n)
     moe = load()
-    T, H, E, K, I = shape
-    El = E // n
+    out = {}
     try:
-        uid = [moe.ep_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        x, _, _ = moe.make_inputs_torch(T, H, E, K, I, 1000 + rank)
-        _, wg, ew = moe.make_inputs_torch(T, H, E, K, I, 7)  # same weights on every rank
-        ref = moe.moe_layer_forward(x, wg, ew, K)
-        ctx = moe.EpContext(uid[0], rank, n, timeout_ms=30000)
-        try:
-            local = ew[rank * El:(rank + 1) * El].contiguous()
-            ws = torch.empty((ctx.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device="cuda")
-            y = ctx.forward(x, wg, local, K, workspace=ws)
-            y2 = ctx.forward(x, wg, local, K, workspace=ws)
-            torch.cuda.synchronize()
-            assert moe.device_error(ws) == 0
-        finally:
-            ctx.close()
-        q.put((rank, bool(torch.equal(y, ref)), bool(torch.equal(y2, ref)), float((y.float() - ref.float()).abs().max())))
+        for path in ("p2p", "nccl"):
+            if path == "nccl":
+                os.environ["MOE_EP_FORCE_NCCL"] = "1"
+            else:
+                os.environ.pop("MOE_EP_FORCE_NCCL", None)
+            uid = [moe.ep_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            ctx = moe.EpContext(uid[0], rank, n, timeout_ms=30000)
+            try:
+                for shape in MULTI_SHAPES:
+                    T, H, E, K, I = shape
+                    El = E // n
+                    x, wg, ew = (torch.from_numpy(a).cuda() for a in _ep_inputs(moe, shape, rank))
+                    ref = moe.moe_layer_forward(x, wg, ew, K)
+                    ids, _ = moe.moe_routing_topk(x, wg, K)
+                    local = ew[rank * El:(rank + 1) * El].contiguous()
+                    ws = torch.empty((ctx.workspace_size(T, H, E, K, I),), dtype=torch.uint8, device="cuda")
+                    y = ctx.forward(x, wg, local, K, workspace=ws)
+                    y2 = ctx.forward(x, wg, local, K, workspace=ws)  # the inboxes are reused
+                    torch.cuda.synchronize()
+                    out[(path, shape)] = dict(
+                        err=moe.device_error(ws), eq1=bool(torch.equal(y, ref)), eq2=bool(torch.equal(y2, ref)),
+                        ids=ids.cpu().numpy(), y=y.cpu().numpy())
+            finally:
+                ctx.close()
+        q.put((rank, out, None))
+    except Exception as exc:  # reported to the parent, which fails the test
+        q.put((rank, out, repr(exc)))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("path", ["p2p", "nccl"])
-@pytest.mark.parametrize("shape", [(300, 256, 8, 2, 512), (1024, 2048, 16, 2, 1024)])
-def test_ep_multi_gpu_matches_layer(shape, path):
-    n = min(torch.cuda.device_count(), 4)
-    if n < 2:
-        pytest.skip("needs 2 GPUs")
-    if shape[2] % n:
-        pytest.skip("E not divisible by the GPU count")
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_ep_multi_gpu_vs_oracle(n, moe, O):
+    """n ranks (one process per GPU), peer-memory and NCCL exchange paths, three
+    shapes: every rank's y equals MoeLayerForward on its tokens bit for bit (two
+    calls in a row), its ids equal the oracle's (tests/moe_cpu_sim.cpp:198-243)
+    away from near ties, and its y rows on Y_TOKENS tokens are within the
+    reference's tolerance of the oracle layer (:249-305) on the ids the GPU chose."""
+    import numpy as np
+
+    from test_gpu_parity import check_close, check_ids
+
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, n, port, shape, path, q)) for r in range(n)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, n, port, q)) for r in range(n)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(n)]
+    res = [q.get(timeout=600) for _ in range(n)]
     for p in procs:
         p.join(timeout=120)
-    for rank, eq1, eq2, err in res:
-        assert eq1 and eq2, (rank, err)
+    for rank, out, exc in res:
+        assert exc is None, (rank, exc)
+        for shape in MULTI_SHAPES:
+            T, H, E, K, I = shape
+            x, wg, ew = (a.astype(np.float32) for a in _ep_inputs(moe, shape, rank))
+            rid, rw, _, _, margin = O.routing(x, wg, K)
+            for path in ("p2p", "nccl"):
+                r = out[(path, shape)]
+                assert r["err"] == 0 and r["eq1"] and r["eq2"], (rank, path, shape, r["err"])
+                check_ids(r["ids"], rid, margin, f"ep{n} rank{rank} {path} T={T} H={H} E={E} K={K} I={I}")
+            sl = np.linspace(0, T - 1, min(Y_TOKENS, T)).astype(np.int64)
+            ids = out[("p2p", shape)]["ids"]
+            ffn = O.expert_ffn(x[sl], ew, ids[sl], I)
+            ok = np.all(ids[sl] == rid[sl], axis=1)
+            yref = O.combine(ffn, rw[sl])
+            for path in ("p2p", "nccl"):
+                check_close(out[(path, shape)]["y"].astype(np.float32)[sl][ok], yref[ok],
+                            f"ep{n} rank{rank} {path} {shape} y")
 
 
 def test_bounded_wait_reports_timeout_and_context_survives(moe):
