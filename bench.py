@@ -132,12 +132,19 @@ def dist_env():
 
 
 # ============================================================================ reference arm
-def reference_inputs(cfg, moe):
-    """The configuration's inputs as fp32 numpy (fp16-rounded values), drawn on the CPU."""
+def reference_inputs(cfg, moe, tensors=None):
+    """The configuration's inputs as fp32 numpy (fp16-rounded values).  `tensors`:
+    the GPU arm's own (x, w_gate, expert_weights); otherwise they are drawn the way
+    the GPU arm draws them (on the GPU when there is one: torch's generator gives a
+    different stream on the CPU)."""
     import numpy as np
+    import torch
 
     T, H, E, K, I, seed = moe.CONFIGS[cfg]
-    x, wg, ew = moe.make_inputs_torch(T, H, E, K, I, seed, device="cpu", zipf=moe.inputs.ZIPF.get(cfg))
+    if tensors is None:
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        tensors = moe.make_inputs_torch(T, H, E, K, I, seed, device=dev, zipf=moe.inputs.ZIPF.get(cfg))
+    x, wg, ew = (t.cpu() for t in tensors)
     return (x.float().numpy(), wg.float().numpy(), ew.float().numpy().astype(np.float32, copy=False)), \
         (T, H, E, K, I)
 
@@ -147,10 +154,10 @@ class CpuReference:
     and TiledMoE (:543-569) from oracle/_ref, or, when that was not built, the C
     restatement of NaiveMoE (oracle/_build; no tiled path)."""
 
-    def __init__(self, cfg, moe):
+    def __init__(self, cfg, moe, tensors=None):
         from oracle import oracle as O
 
-        (self.x, self.wg, self.ew), self.shape = reference_inputs(cfg, moe)
+        (self.x, self.wg, self.ew), self.shape = reference_inputs(cfg, moe, tensors)
         self.O = O
         self.kind = "reference" if O.ref_available() else "port"
         self.t = O.RefTimer(self.x, self.wg, self.ew, self.shape[3]) if self.kind == "reference" else None
@@ -223,7 +230,7 @@ def run_reference(args):
 
 
 # ============================================================================ our arm
-def cpu_baseline_sample(args, moe, ids_gpu=None):
+def cpu_baseline_sample(args, moe, tensors, ids_gpu=None):
     """The reference's CPU code on a bounded sample of the same workload (rank 0,
     N=1): NaiveMoE on successive slices of the batch until at least --cpu-seconds,
     then TiledMoE for a third of that; tokens/s over each whole sample.  Also the
@@ -232,7 +239,7 @@ def cpu_baseline_sample(args, moe, ids_gpu=None):
     apart (the reference's own tie order is unspecified, tests/moe_cpu_sim.cpp:232-233)."""
     import numpy as np
 
-    ref = CpuReference(args.config, moe)
+    ref = CpuReference(args.config, moe, tensors)
     T, H, E, K, I = ref.shape
     threads = os.cpu_count() or 1
     chunk = max(1, min(args.ref_tokens, T))
@@ -369,8 +376,10 @@ def run_ours(args):
     # all experts on the same tokens (bit for bit: every kernel is the same)
     ep_parity = None
     if world > 1:
+        # the single-GPU call gets the rank's whole batch: the routing kernel's split of
+        # H over a CTA cluster (hence its fp32 sum order) depends on T
         S = min(256, T)
-        y_one = moe.moe_layer_forward(x[:S].contiguous(), wg, ew_full, K)
+        y_one = moe.moe_layer_forward(x, wg, ew_full, K)[:S]
         torch.cuda.synchronize()
         eq = torch.tensor([float(torch.equal(y_one, y[:S])), float((y_one.float() - y[:S].float()).abs().max())],
                           dtype=torch.float64, device=dev)
@@ -393,6 +402,8 @@ def run_ours(args):
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
 
+    host_ms = [0.0]  # host time to enqueue the last e2e run
+
     def e2e_run(nsteps, compute=True):
         in_ready = [ev(), ev()]
         x_free = [None, None]   # compute finished reading x_dev[b]
@@ -401,6 +412,7 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        host0 = time.perf_counter()
         t_start.record(h2d)
         with torch.cuda.stream(h2d):
             x_dev[0].copy_(x_host[0], non_blocking=True)
@@ -430,13 +442,19 @@ def run_ours(args):
             y_free[b].record(d2h)
         h2d.wait_stream(d2h)
         t_end.record(h2d)
+        host_ms[0] = (time.perf_counter() - host0) * 1e3
         torch.cuda.synchronize()
         return t_start.elapsed_time(t_end)
 
-    mean_ms = total_ms / args.steps
+    # every rank must make the same number of layer calls (the expert-parallel
+    # exchange pairs call c of every rank), so the step counts below come from the
+    # step time agreed over the ranks
+    mean_ms = _max_over_ranks([total_ms / args.steps], world, dev)[0]
     e2e_steps = max(args.steps, int(args.e2e_seconds * 1000.0 / max(mean_ms, 1e-3)) + 1)
     e2e_run(args.warmup)
     e2e_ms = e2e_run(e2e_steps)
+    e2e_host_ms = host_ms[0]
+    e2e_err = moe.device_error(ws)
     # the host-copy ceiling: the same copies on the same streams with no layer
     copy_ms = e2e_run(e2e_steps, compute=False)
     h2d_ms = _copy_only(x_host[0], x_dev[0], h2d, e2e_steps, world)
@@ -458,7 +476,10 @@ def run_ours(args):
             torch.cuda.synchronize()
             sus_stages = moe.trace_stop(20)
         sus = {"steps": sus_steps, "ms_total": sum(sus_ms), "clk": clk_sus.summary(),
-               "g1_ms": statistics.mean(c["gemm_swiglu"] for c in sus_stages)}
+               "g1_ms": statistics.mean(c["gemm_swiglu"] for c in sus_stages),
+               "median_step_ms": statistics.median(sus_ms), "max_step_ms": max(sus_ms),
+               "steps_over_2x_median": sum(1 for m in sus_ms if m > 2 * statistics.median(sus_ms)),
+               "device_error": moe.device_error(ws)}
 
     # ---- strong scaling record (N>1): the config's one batch of T tokens split over
     # the N ranks, same process; efficiency against rank 0's single-GPU layer on the
@@ -544,6 +565,7 @@ def run_ours(args):
                            "two copy streams overlapping the neighbouring steps' compute; ranks start "
                            "together (barrier); max over ranks",
                     "copy_only_ceiling": world * T * e2e_steps / (copy_ms / 1e3),
+                    "host_enqueue_ms_rank0": e2e_host_ms, "device_error_rank0": e2e_err,
                     "per_rank_copy_gbs": [{"h2d": xbytes * e2e_steps / (c[0].item() / 1e3) / 1e9,
                                            "d2h": xbytes * e2e_steps / (c[1].item() / 1e3) / 1e9} for c in copies]},
             # per step, one GPU: routing, fused permute, gather, gate/up GEMM, down GEMM,
@@ -558,6 +580,9 @@ def run_ours(args):
             sv = world * T * sus["steps"] / (sus["ms_total"] / 1e3)
             g1s = g1_flops / (sus["g1_ms"] / 1e3) / 1e12
             line["sustained"] = {"value": sv, "unit": "tokens/s", "steps": sus["steps"],
+                                 "median_step_ms_rank0": sus["median_step_ms"], "max_step_ms_rank0": sus["max_step_ms"],
+                                 "steps_over_2x_median_rank0": sus["steps_over_2x_median"],
+                                 "device_error_rank0": sus["device_error"],
                                  "seconds": sus["ms_total"] / 1e3, "clocks": sus["clk"],
                                  "gemm_swiglu_tflops": g1s,
                                  "gemm_swiglu_frac_of_sustained": g1s / peak_sus if peak_sus else None,
@@ -568,7 +593,7 @@ def run_ours(args):
             line["strong"] = strong
         if world == 1 and not args.no_cpu_baseline:
             try:
-                line["cpu_baseline"] = cpu_baseline_sample(args, moe, ids_gpu=ids_chk.cpu().numpy())
+                line["cpu_baseline"] = cpu_baseline_sample(args, moe, (x, wg, ew), ids_gpu=ids_chk.cpu().numpy())
             except Exception as exc:  # reported, never fatal for the GPU number
                 line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
         print(json.dumps(line), flush=True)

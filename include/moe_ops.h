@@ -145,7 +145,11 @@ int MoeEpDestroy(MoeEpContext* ctx);
 size_t MoeEpWorkspaceSize(int nranks, int64_t numTokens, int64_t hiddenSize, int64_t numExperts,
                           int64_t topK, int64_t intermediateSize, int64_t maxRecvRows);
 
-/* x [T,H] (this rank's tokens), w_gate [H,E] (all experts), expert_weights_local
+/* Every rank makes the same sequence of calls with the same shapes: call c of one
+ * rank exchanges rows with call c of every other rank.  A call whose device error
+ * word reports a timed-out wait (64/128/256) leaves the ranks' call counters out of
+ * step; destroy the context and build a new one.
+ * x [T,H] (this rank's tokens), w_gate [H,E] (all experts), expert_weights_local
  * [E/n, 3I, H] -> y [T,H].  Synchronises the host once per call, on the exchanged
  * row counts (bounded by the context's timeout).  Returns MOE_ERR_WORKSPACE_TOO_SMALL
  * if more rows than maxRecvRows arrive (nothing is written past the workspace). */
