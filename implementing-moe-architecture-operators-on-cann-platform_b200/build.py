@@ -19,9 +19,9 @@ HEADERS = ["moe_common.cuh", "moe_kernels.h"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-         "--expt-relaxed-constexpr", "-Xptxas", "-v"] if os.environ.get("MOE_PTXAS_VERBOSE") else \
-        ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
+if os.environ.get("MOE_PTXAS_VERBOSE"):  # registers / spills / shared memory per kernel
+    FLAGS = FLAGS + ["-Xptxas", "-v"]
 # extra compile definitions, e.g. MOE_NVCC_EXTRA="-DMOE_GEMM_STAGES=3" (tuning builds)
 FLAGS = FLAGS + os.environ.get("MOE_NVCC_EXTRA", "").split()
 

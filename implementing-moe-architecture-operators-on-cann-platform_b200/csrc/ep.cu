@@ -632,7 +632,7 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
         moe::trace_mark(ev, 4, s);
         // GEMM2 writes row r of expert order to recv[row_src[r]] (source-major order)
         e = moe::launch_gemm_down(hbuf, static_cast<const __half*>(expert_weights_local), expoff, row_src, recv, err,
-                                  rows, (int)H, El, (int)I, 0, s, kEpRowsHint);
+                                  rows, (int)H, El, (int)I, 0, s, rows, false);
         if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
         if (e != cudaSuccess) return MOE_ERR_CUDA;
     }
@@ -851,7 +851,7 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     e = moe::launch_gemm_down_ptr(hbuf, static_cast<const __half*>(ewl), expoff, row_ptr, done2,
                                   reinterpret_cast<unsigned long long* const*>(
                                       reinterpret_cast<const uint8_t*>(dp) + offsetof(EpPeers, ret_flag)),
-                                  n, err, (int)R, (int)H, El, (int)I, s, kEpRowsHint);
+                                  n, err, (int)R, (int)H, El, (int)I, s, (int)(T * K), false);
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 5, s);

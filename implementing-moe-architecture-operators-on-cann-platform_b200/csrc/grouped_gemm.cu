@@ -95,13 +95,24 @@ struct GemmArgs {
 #endif
 constexpr int GM_MAX_STAGES = 8;
 
-template <int PAIR>
+// Narrow tiles (BN=128, single-CTA, down projection only): one 128-row box of B per
+// stage, N=128 UMMAs.  Used when the problem has fewer wide tiles than SMs (few
+// rows per launch: expert-parallel ranks, decode); each output element's
+// accumulation over k is the same UMMA chain as with wide tiles.
+#ifndef MOE_GEMM_NARROW_STAGES
+#define MOE_GEMM_NARROW_STAGES 6
+#endif
+
+template <int PAIR, int BN = GM_BN>
 struct GemmCfg {
-    static constexpr int STAGES = PAIR ? MOE_GEMM_PAIR_STAGES : GM_STAGES;
-    static constexpr int STAGE_BYTES = PAIR ? GM_A_BYTES + GM_BHALF_BYTES : GM_STAGE_BYTES;
+    static_assert(BN == GM_BN || (BN == 128 && !PAIR), "narrow tiles are single-CTA only");
+    static constexpr int STAGES = PAIR ? MOE_GEMM_PAIR_STAGES : (BN == 128 ? MOE_GEMM_NARROW_STAGES : GM_STAGES);
+    static constexpr int STAGE_BYTES =
+        PAIR ? GM_A_BYTES + GM_BHALF_BYTES : (BN == 128 ? GM_A_BYTES + GM_BHALF_BYTES : GM_STAGE_BYTES);
     static constexpr int ROWS = PAIR ? 2 * GM_BM : GM_BM;  // rows of one tile (over the pair)
 };
-static_assert(GemmCfg<0>::STAGES <= GM_MAX_STAGES && GemmCfg<1>::STAGES <= GM_MAX_STAGES, "stages");
+static_assert(GemmCfg<0>::STAGES <= GM_MAX_STAGES && GemmCfg<1>::STAGES <= GM_MAX_STAGES &&
+                  GemmCfg<0, 128>::STAGES <= GM_MAX_STAGES, "stages");
 
 struct GemmSmemTail {
     uint64_t full[GM_MAX_STAGES];
@@ -119,13 +130,14 @@ struct GemmSmemTail {
 constexpr int GM_STG_ROW = 80;
 constexpr int GM_STG_BYTES = 4 * 32 * GM_STG_ROW;
 
-template <int PAIR>
+template <int PAIR, int BN = GM_BN>
 __host__ __device__ constexpr size_t gemm_smem_bytes()
 {
-    return 1024 + (size_t)GemmCfg<PAIR>::STAGES * GemmCfg<PAIR>::STAGE_BYTES +
+    return 1024 + (size_t)GemmCfg<PAIR, BN>::STAGES * GemmCfg<PAIR, BN>::STAGE_BYTES +
            ((sizeof(GemmSmemTail) + 127) & ~(size_t)127) + GM_STG_BYTES;
 }
-static_assert(gemm_smem_bytes<0>() <= 227 * 1024 && gemm_smem_bytes<1>() <= 227 * 1024, "smem");
+static_assert(gemm_smem_bytes<0>() <= 227 * 1024 && gemm_smem_bytes<1>() <= 227 * 1024 &&
+                  gemm_smem_bytes<0, 128>() <= 227 * 1024, "smem");
 
 // Stores one 32-column chunk (64 bytes) of each of the warp's 32 rows.  Each
 // thread parks its row's chunk in shared memory (rows padded to 80 bytes so the
@@ -179,12 +191,13 @@ struct TileCursor {
     }
 };
 
-template <int MODE, int PAIR>
+template <int MODE, int PAIR, int BN>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmArgs args)
 {
-    using Cfg = GemmCfg<PAIR>;
+    static_assert(BN == GM_BN || MODE != MODE_SWIGLU, "GEMM1 tiles carry 128 gate + 128 up columns");
+    using Cfg = GemmCfg<PAIR, BN>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr int STAGE_BYTES = Cfg::STAGE_BYTES;
     constexpr int ROWS = Cfg::ROWS;
@@ -298,8 +311,9 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         mbar_arrive_expect_tx(full, STAGE_BYTES);
                         tma_load_2d(smem_u32(st), &tmA, full, kb * GM_BK, a_row, pol_a);
                         tma_load_2d(smem_u32(st + GM_A_BYTES), &tmB, full, kb * GM_BK, b_lo, pol_b);
-                        tma_load_2d(smem_u32(st + GM_A_BYTES + GM_BHALF_BYTES), &tmB, full, kb * GM_BK,
-                                    b_hi, pol_b);
+                        if (BN == GM_BN)
+                            tma_load_2d(smem_u32(st + GM_A_BYTES + GM_BHALF_BYTES), &tmB, full, kb * GM_BK,
+                                        b_hi, pol_b);
                     }
                 }
             }
@@ -320,7 +334,7 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = umma_idesc_f16_f32(ROWS, GM_BN);
+            constexpr uint32_t idesc = umma_idesc_f16_f32(ROWS, BN);
             uint32_t it = 0, lt = 0;
             bool ok = true;
             for (int tile = unit; ok && tile < total_tiles; tile += nunits, lt++) {
@@ -453,7 +467,7 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     }
                 }
             } else {
-                const int col0 = nt * GM_BN;
+                const int col0 = nt * BN;
                 __half* dst = nullptr;
                 if (valid) {
                     if (MODE == MODE_DOWN_PTR)
@@ -462,7 +476,7 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         dst = args.out + (size_t)args.perm[row0 + r] * args.out_ld + col0;
                 }
 #pragma unroll 1
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < BN / 32; j++) {
                     uint32_t v32[32];
                     tmem_ld_32x32b_x32(tbase + j * 32, v32);
                     tmem_ld_wait();
@@ -567,16 +581,16 @@ static int sm_count()
     return n[dev];
 }
 
-template <int MODE, int PAIR>
+template <int MODE, int PAIR, int BN>
 static cudaError_t set_gemm_attr()
 {
     static bool done[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_kernel<MODE, PAIR>,
+    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_kernel<MODE, PAIR, BN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)gemm_smem_bytes<PAIR>());
+                                         (int)gemm_smem_bytes<PAIR, BN>());
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
 }
@@ -605,11 +619,11 @@ static bool use_pair(int rows_cap, int E)
     return E > 0 && rows_cap / E >= 1536;
 }
 
-template <int MODE, int PAIR>
+template <int MODE, int PAIR, int BN = GM_BN>
 static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int rows_cap,
                               int max_ctas, bool pdl, cudaStream_t s)
 {
-    cudaError_t e = set_gemm_attr<MODE, PAIR>();
+    cudaError_t e = set_gemm_attr<MODE, PAIR, BN>();
     if (e != cudaSuccess) return e;
     int grid;
     if (PAIR) {
@@ -625,7 +639,7 @@ static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, cons
             cudaLaunchConfig_t q = {};
             q.gridDim = dim3(2 * (sm_count() / 2));
             q.blockDim = dim3(GM_THREADS);
-            q.dynamicSmemBytes = gemm_smem_bytes<PAIR>();
+            q.dynamicSmemBytes = gemm_smem_bytes<PAIR, BN>();
             cudaLaunchAttribute ca;
             ca.id = cudaLaunchAttributeClusterDimension;
             ca.val.clusterDim.x = 2;
@@ -634,7 +648,7 @@ static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, cons
             q.attrs = &ca;
             q.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, ffn_gemm_kernel<MODE, PAIR>, &q) != cudaSuccess || n <= 0) {
+            if (cudaOccupancyMaxActiveClusters(&n, ffn_gemm_kernel<MODE, PAIR, BN>, &q) != cudaSuccess || n <= 0) {
                 cudaGetLastError();
                 n = sm_count() / 2;
             }
@@ -651,7 +665,7 @@ static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, cons
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(grid);
     lc.blockDim = dim3(GM_THREADS);
-    lc.dynamicSmemBytes = gemm_smem_bytes<PAIR>();
+    lc.dynamicSmemBytes = gemm_smem_bytes<PAIR, BN>();
     lc.stream = s;
     cudaLaunchAttribute at[2];
     int na = 0;
@@ -669,7 +683,7 @@ static cudaError_t launch_ffn(const CUtensorMap& ta, const CUtensorMap& tb, cons
     }
     lc.attrs = at;
     lc.numAttrs = na;
-    e = cudaLaunchKernelEx(&lc, ffn_gemm_kernel<MODE, PAIR>, ta, tb, a);
+    e = cudaLaunchKernelEx(&lc, ffn_gemm_kernel<MODE, PAIR, BN>, ta, tb, a);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -679,6 +693,41 @@ static cudaError_t launch_ffn_any(const CUtensorMap& ta, const CUtensorMap& tb, 
                                   int rows_hint, int max_ctas, bool pdl, cudaStream_t s)
 {
     if (use_pair(rows_hint >= 0 ? rows_hint : rows_cap, a.E)) return launch_ffn<MODE, 1>(ta, tb, a, rows_cap, max_ctas, pdl, s);
+    return launch_ffn<MODE, 0>(ta, tb, a, rows_cap, max_ctas, pdl, s);
+}
+
+// Down projection: narrow (BN=128) tiles when all of them fit in one wave (twice the
+// wide tiles <= SMs), i.e. when the wide tiles would leave half the SMs idle.
+// Measured (one B200): 2 experts x 512 rows, H=2048, I=8192: 53 us narrow against
+// 64 us wide; 4 experts x 512 rows (two narrow waves): 96 against 68; decode (16
+// experts x 16 rows, HBM-bound): 110 against 106.  rows: the expected permuted
+// rows; the m tiles are estimated as rows/128 plus half a tail tile per expert.
+// MOE_GEMM_DOWN_BN=128/256 forces the width.
+static bool use_narrow_down(int rows, int E, int H, bool pair)
+{
+    static int forced = -1;
+    if (forced == -1) {
+        const char* v = getenv("MOE_GEMM_DOWN_BN");
+        forced = v ? atoi(v) : 0;
+    }
+    if (forced == 128) return true;
+    if (forced == 256 || pair) return false;
+    const long long wide = (long long)((H + GM_BN - 1) / GM_BN) * (rows / GM_BM + (E + 1) / 2);
+    return 2 * wide <= sm_count();
+}
+
+template <int MODE>
+static cudaError_t launch_down_any(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs a, int rows_cap, int rows_hint, bool allow_pair, int max_ctas,
+                                   bool pdl, cudaStream_t s)
+{
+    const int rows = rows_hint >= 0 ? rows_hint : rows_cap;
+    const bool pair = allow_pair && use_pair(rows, a.E);
+    if (!pair && use_narrow_down(rows, a.E, a.nvalid, false)) {
+        a.n_tiles = (a.nvalid + 127) / 128;
+        a.b_nstep = 128;
+        return launch_ffn<MODE, 0, 128>(ta, tb, a, rows_cap, max_ctas, pdl, s);
+    }
+    if (pair) return launch_ffn<MODE, 1>(ta, tb, a, rows_cap, max_ctas, pdl, s);
     return launch_ffn<MODE, 0>(ta, tb, a, rows_cap, max_ctas, pdl, s);
 }
 
@@ -711,7 +760,7 @@ cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, c
 // GEMM2: expert_out[perm[r], :] = h[r, :] @ Wd^T per expert.
 cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
                              const int32_t* perm, __half* expert_out, int* err, int rows_cap, int H,
-                             int E, int I, int max_ctas, cudaStream_t s, int rows_hint)
+                             int E, int I, int max_ctas, cudaStream_t s, int rows_hint, bool allow_pair)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
@@ -731,7 +780,7 @@ cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, cons
     a.b_nstep = GM_BN;
     a.b_hi_delta = 128;
     a.out_ld = H;
-    return launch_ffn_any<MODE_DOWN>(ta, tb, a, rows_cap, rows_hint, max_ctas, true, s);
+    return launch_down_any<MODE_DOWN>(ta, tb, a, rows_cap, rows_hint, allow_pair, max_ctas, true, s);
 }
 
 }  // namespace moe
@@ -743,7 +792,7 @@ namespace moe {
 cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, const int32_t* offsets,
                                  const unsigned long long* row_ptr, unsigned int* done_counter,
                                  unsigned long long* const* peer_flags, int npeers, int* err, int rows_cap,
-                                 int H, int E, int I, cudaStream_t s, int rows_hint)
+                                 int H, int E, int I, cudaStream_t s, int rows_hint, bool allow_pair)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, h, (uint64_t)I, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
@@ -765,7 +814,7 @@ cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, 
     a.done_counter = done_counter;
     a.peer_flags = peer_flags;
     a.npeers = npeers;
-    return launch_ffn_any<MODE_DOWN_PTR>(ta, tb, a, rows_cap, rows_hint, 0, false, s);
+    return launch_down_any<MODE_DOWN_PTR>(ta, tb, a, rows_cap, rows_hint, allow_pair, 0, false, s);
 }
 
 }  // namespace moe

@@ -47,14 +47,16 @@ cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32
 
 // Grouped GEMM launchers.  rows_cap bounds the permuted rows (the A tensor's
 // extent); rows_hint, when >= 0, is the expected number of rows actually present
-// (used only to choose between single-CTA and paired-CTA tiles).
+// (used only to choose the tile shape: single-CTA or paired-CTA tiles, and for the
+// down projection wide or narrow ones); allow_pair = false keeps single-CTA tiles.
 cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights,
                                const int32_t* offsets, __half* h, int* err, int rows_cap, int H,
                                int E, int I, int max_ctas, cudaStream_t s, int rows_hint = -1);
 
 cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
                              const int32_t* perm, __half* expert_out, int* err, int rows_cap,
-                             int H, int E, int I, int max_ctas, cudaStream_t s, int rows_hint = -1);
+                             int H, int E, int I, int max_ctas, cudaStream_t s, int rows_hint = -1,
+                             bool allow_pair = true);
 
 cudaError_t launch_combine_indexed(const __half* rows, const int32_t* dest, const __half* weights,
                                    __half* y, int T, int H, int K, cudaStream_t s);
@@ -70,7 +72,7 @@ void trace_mark(cudaEvent_t* ev, int boundary, cudaStream_t s);
 cudaError_t launch_gemm_down_ptr(const __half* h, const __half* expert_weights, const int32_t* offsets,
                                  const unsigned long long* row_ptr, unsigned int* done_counter,
                                  unsigned long long* const* peer_flags, int npeers, int* err, int rows_cap,
-                                 int H, int E, int I, cudaStream_t s, int rows_hint = -1);
+                                 int H, int E, int I, cudaStream_t s, int rows_hint = -1, bool allow_pair = true);
 
 cudaError_t launch_combine(const __half* expert_out, const __half* weights, __half* y, int T,
                            int H, int K, cudaStream_t s);
