@@ -570,8 +570,8 @@ def run_ours(args):
                                            "d2h": xbytes * e2e_steps / (c[1].item() / 1e3) / 1e9} for c in copies]},
             # per step, one GPU: routing, fused permute, gather, gate/up GEMM, down GEMM,
             # combine; expert parallel: routing, permute, counts, plan, dispatch,
-            # row-pointer, rows wait, gate/up GEMM, down GEMM, return wait, combine
-            "gpu_launches": args.steps * (11 if world > 1 else 6),
+            # row-pointer, gate/up GEMM (waits per source), down GEMM, combine on arrival
+            "gpu_launches": args.steps * (9 if world > 1 else 6),
             "clocks": clk.summary(),
         }
         if ep_parity is not None:

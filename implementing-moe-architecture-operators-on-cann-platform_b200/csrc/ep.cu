@@ -1,28 +1,32 @@
-// ep.cu -- the MoE layer expert-parallel over n GPUs with NCCL send/recv.
+// ep.cu -- the MoE layer expert-parallel over n GPUs.
 //
 // The reference runs on one device (tests/test_moe.cpp:642-648); the benchmark
 // definition asks for the layer partitioned expert-parallel across the GPUs of a
-// box.  Rank r owns experts [r*El, (r+1)*El), El = E/n, and routes its own tokens:
+// box.  Rank r owns experts [r*El, (r+1)*El), El = E/n, and routes its own tokens.
 //
+// Peer-memory path (default, one process per GPU, n <= 8; no host synchronisation):
 //   1. routing + stable counting sort of this rank's (token, slot) pairs by expert
 //      (experts are owned contiguously, so expert order is also owner order);
-//   2. gather of the permuted rows xp [T*K, H];
-//   3. exchange of per-(owner, expert) row counts (NCCL send/recv of El ints per
-//      peer), one bounded host wait on them, host plan (MoeEpPlan);
-//   4. dispatch: grouped ncclSend/ncclRecv of row blocks, into recv [R, H] in
-//      source-major order;
-//   5. reorder to expert-major (copy_rows), grouped GEMM1 (gate/up + SwiGLU) and
-//      GEMM2 (down) on the local experts; GEMM2 scatters each row back to its
-//      source-major slot, so no second reorder is needed;
-//   6. return: the mirrored send/recv into ret [T*K, H] (this rank's permuted order);
-//   7. combine through the permutation's inverse (combine_indexed).
-// Every kernel is the single-GPU one, so each row of y is bit-identical to
-// MoeLayerForward on the same tokens with all experts.  Remote rows reach local
-// HBM through NCCL before any kernel reads them; no kernel reads peer memory.
+//   2. per-expert counts stored into every peer's inbox, then a device-side plan
+//      once every source's counts are in;
+//   3. fused gather + dispatch: each row goes from x straight into its owner's
+//      inbox over NVLink; GEMM1 (gate/up + SwiGLU) runs alongside it, each tile
+//      waiting only for the sources whose rows it covers;
+//   4. GEMM2 (down) stores every output row straight into its source rank's
+//      return inbox and raises this owner's flag there;
+//   5. combine on arrival: tokens whose owners have all returned their rows first.
+// NCCL path (fallback, or MOE_EP_FORCE_NCCL=1): counts exchange with one bounded
+// host wait, grouped ncclSend/ncclRecv dispatch and return, an expert-major reorder,
+// the same GEMMs, combine through the inverse permutation.
+// Every kernel computes each row exactly as the single-GPU path does, so each row
+// of y is bit-identical to MoeLayerForward on the same tokens with all experts.
+// No kernel reads peer memory with TMA or with cluster multicast: remote data is
+// written with plain stores and read from local HBM.
 //
-// Failure handling: the communicator is non-blocking; every wait (communicator
+// Failure handling: the communicator is non-blocking; every host wait (communicator
 // set-up, group completion, the counts event) polls against a deadline and aborts
-// the communicator on timeout, returning MOE_ERR_TIMEOUT instead of hanging.
+// the communicator on timeout, returning MOE_ERR_TIMEOUT instead of hanging.  Every
+// device wait on a peer's flag is bounded and records an error bit.
 #include <nccl.h>
 #include <stddef.h>
 #include <stdlib.h>
@@ -188,67 +192,60 @@ __global__ void ep_row_map_kernel(const int32_t* __restrict__ seg, int nseg, int
 
 // ============================================================================ peer-memory path
 // One allocation per rank, shared with the peers through CUDA IPC:
-//   cnt   [n][E] int32   row s: source s's per-expert row counts (written by s)
+//   flags [32] u64       per-source epoch counters, each raised by one rank once per
+//                        call: [s] counts of source s are in, [8+s] rows of source s
+//                        have landed, [16+o] owner o's returned rows have landed;
+//                        [24]/[25]: local completion counters (u32) of the dispatch
+//                        kernel and the down GEMM
+//   cnt   [2][n][E] int32  row s of buffer (call & 1): source s's per-expert counts
 //   rows  [R][H] fp16    rows for this rank's experts, expert-major (written by sources)
 //   ret   [T*K][H] fp16  this rank's rows back from their experts, in permuted order
-//   flags [8] u64        0: counts, 1: rows, 2: ret -- each source adds 1 per call;
-//                        4/5: local completion counters of the dispatch kernel (u32)
-// Every flag only grows, so "call number c is complete" is flag >= c * n.
+// Call c waits for flag >= c.  A counter only grows, and it is per source, so a fast
+// rank's call c+1 never satisfies a wait for a slow rank's call c.  The counts are
+// double-buffered by call parity: a rank can run one call ahead of a peer's plan
+// (its combine waits only for the owners its own tokens used), never two, because
+// its next plan needs that peer's next counts.
 constexpr int EP_MAX_PEERS = 8;
+constexpr int F_CNT = 0, F_ROWS = 8, F_RET = 16, F_DONE1 = 24, F_DONE2 = 25, F_WORDS = 32;
 
 struct EpPeers {
     int32_t* cnt[EP_MAX_PEERS];
     __half* rows[EP_MAX_PEERS];
     __half* ret[EP_MAX_PEERS];
     unsigned long long* flags[EP_MAX_PEERS];
-    unsigned long long* ret_flag[EP_MAX_PEERS];  // &flags[p][2], for the GEMM2 signal
+    unsigned long long* ret_flag[EP_MAX_PEERS];  // &flags[p][F_RET + me], for the GEMM2 signal
 };
 
 enum EpDevError { EP_ERR_WAIT_COUNTS = 64, EP_ERR_WAIT_ROWS = 128, EP_ERR_WAIT_RET = 256, EP_ERR_OVERFLOW = 512 };
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
-{
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // Bounded wait (one thread) until *flag >= target; on timeout records `code`.
 __device__ bool ep_wait_flag(const unsigned long long* flag, unsigned long long target, int* err, int code)
 {
-    if (ld_acquire_sys(flag) >= target) return true;
-    const uint64_t t0 = moe::global_timer_ns();
-    for (;;) {
-        if (ld_acquire_sys(flag) >= target) return true;
-        if (moe::global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) {
-            atomicOr(err, code);
-            return false;
-        }
-        __nanosleep(64);
-    }
+    return moe::flag_wait_bounded(flag, target, err, code, nullptr);
 }
 
-// Writes this rank's per-expert counts into row `me` of every peer's cnt inbox,
-// then signals each peer's counts flag.
+// Writes this rank's per-expert counts into row `me` of buffer `par` of every
+// peer's cnt inbox, then raises its counts flag there.
 __global__ void ep_p2p_counts_kernel(const EpPeers* __restrict__ peers, const int32_t* __restrict__ offsets, int E,
-                                     int me, int n)
+                                     int me, int n, int par)
 {
     for (int p = 0; p < n; p++)
-        for (int e = threadIdx.x; e < E; e += blockDim.x) peers->cnt[p][me * E + e] = offsets[e + 1] - offsets[e];
+        for (int e = threadIdx.x; e < E; e += blockDim.x)
+            peers->cnt[p][((size_t)par * n + me) * E + e] = offsets[e + 1] - offsets[e];
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x < n) {
         __threadfence_system();
-        atomicAdd_system(&peers->flags[threadIdx.x][0], 1ull);
+        atomicAdd_system(&peers->flags[threadIdx.x][F_CNT + me], 1ull);
     }
 }
 
 // Plan, on the device, once every source's counts are in: for each global expert e
 // the row in its owner's inbox where this rank's rows start (disp_base[e]); this
 // rank's expert-major offsets (expoff[El+1]) and, for each (local expert, source),
-// {first inbox row, rows, row index in the source's permuted order} (seg).
-__global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt, const unsigned long long* flags, int E, int El,
-                                   int me, int n, int R, unsigned long long target, int* err,
+// {first inbox row, row index in the source's permuted order, rows} (seg).
+__global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt_all, const unsigned long long* flags, int E,
+                                   int El, int me, int n, int par, int R, unsigned long long target, int* err,
                                    int32_t* __restrict__ disp_base, int32_t* __restrict__ expoff,
                                    int32_t* __restrict__ seg, int32_t* __restrict__ overflow)
 {
@@ -256,10 +253,13 @@ __global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt, const unsign
     __shared__ int over;
     extern __shared__ int32_t pl_tot[];  // [E] rows per global expert over all sources
     if (threadIdx.x == 0) {
-        ok = ep_wait_flag(&flags[0], target, err, EP_ERR_WAIT_COUNTS);
+        int good = 1;
+        for (int s = 0; s < n && good; s++) good = ep_wait_flag(&flags[F_CNT + s], target, err, EP_ERR_WAIT_COUNTS);
+        ok = good;
         over = 0;
     }
     __syncthreads();
+    const int32_t* cnt = cnt_all + (size_t)par * n * E;
     if (!ok) {  // counts never arrived: plan nothing, move nothing
         for (int i = threadIdx.x; i <= El; i += blockDim.x) expoff[i] = 0;
         for (int i = threadIdx.x; i < El * n; i += blockDim.x) seg[3 * i + 2] = 0;
@@ -312,14 +312,17 @@ __global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt, const unsign
 
 // Fused gather + dispatch: row r of this rank's permuted order (expert e) goes from
 // x[perm[r]/K] straight to its owner's inbox row disp_base[e] + (r - offsets[e]),
-// over NVLink for remote owners.  The last block to finish signals every peer's
-// rows flag.
+// over NVLink for remote owners.  The last block to finish raises this rank's
+// rows flag at every peer.  It lets the GEMM1 launch after it start at once (that
+// kernel reads the rows only behind their flags) and runs on a small grid, so the
+// GEMM1 CTAs fit on the SMs beside its blocks.
 __global__ void __launch_bounds__(256)
 ep_p2p_dispatch_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
                        const int32_t* __restrict__ offsets, const int32_t* __restrict__ disp_base,
                        const int32_t* __restrict__ overflow, const EpPeers* __restrict__ peers, int TK, int E,
-                       int El, int K, int H, int n, unsigned int* done)
+                       int El, int K, int H, int me, int n, unsigned int* done)
 {
+    moe::pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int nv = H >> 3;
     if (!*overflow) {
@@ -344,7 +347,7 @@ ep_p2p_dispatch_kernel(const __half* __restrict__ x, const int32_t* __restrict__
         if (old == gridDim.x - 1) {
             *reinterpret_cast<volatile unsigned int*>(done) = 0u;
             __threadfence_system();
-            for (int p = 0; p < n; p++) atomicAdd_system(&peers->flags[p][1], 1ull);
+            for (int p = 0; p < n; p++) atomicAdd_system(&peers->flags[p][F_ROWS + me], 1ull);
         }
     }
 }
@@ -363,10 +366,92 @@ __global__ void ep_p2p_rowptr_kernel(const int32_t* __restrict__ seg, int nseg, 
     }
 }
 
-// Waits (bounded) until every source's rows have landed in this rank's inbox.
+// Waits (bounded) until *flag >= target (the failure-detection self-test).
 __global__ void ep_p2p_wait_kernel(const unsigned long long* flag, unsigned long long target, int* err, int code)
 {
     if (threadIdx.x == 0) ep_wait_flag(flag, target, err, code);
+}
+
+// Combine on arrival.  Block b owns tokens [b*CH, b*CH+CH).  Slot (t,k) comes back
+// from owner ids[t,k]/El, whose rows are all in once ret_flags[owner] >= target.
+// The block first combines the tokens whose owners have all signalled, then waits
+// (bounded) for the missing owners of the rest, so tokens that do not need a slow
+// owner are not held up by it.  Each token is the same fp32 sum in slot order as
+// combine_indexed_kernel (tests/moe_cpu_sim.cpp:298-305), so y is bit-identical.
+constexpr int EP_COMBINE_CH = 16;
+
+__global__ void __launch_bounds__(256)
+ep_combine_arrival_kernel(const __half* __restrict__ ret, const int32_t* __restrict__ dest,
+                          const int32_t* __restrict__ ids, const __half* __restrict__ weights,
+                          __half* __restrict__ y, int T, int H, int K, int El, int n,
+                          const unsigned long long* ret_flags, unsigned long long target, int* err)
+{
+    __shared__ uint32_t need[EP_COMBINE_CH];
+    __shared__ int order[EP_COMBINE_CH];
+    __shared__ int n_ready;
+    __shared__ uint32_t ready;
+    const int t0 = blockIdx.x * EP_COMBINE_CH;
+    const int cnt = min(EP_COMBINE_CH, T - t0);
+    if (threadIdx.x < cnt) {
+        uint32_t m = 0;
+        for (int k = 0; k < K; k++) {
+            const int e = ids[(size_t)(t0 + threadIdx.x) * K + k];
+            if (e >= 0 && e < El * n) m |= 1u << (e / El);  // a bad id was reported by the permutation
+        }
+        need[threadIdx.x] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t all = 0, rd = 0;
+        for (int i = 0; i < cnt; i++) all |= need[i];
+        for (int o = 0; o < 32; o++)  // one look at each owner this block needs
+            if (((all >> o) & 1u) && moe::ld_acquire_sys(&ret_flags[o]) >= target) rd |= 1u << o;
+        int j = 0;
+        for (int i = 0; i < cnt; i++)
+            if (!(need[i] & ~rd)) order[j++] = i;
+        n_ready = j;
+        for (int i = 0; i < cnt; i++)
+            if (need[i] & ~rd) order[j++] = i;
+        ready = rd;
+    }
+    __syncthreads();
+    const int vpr = H >> 3;
+    for (int j = 0; j < cnt; j++) {
+        const int i = order[j];
+        if (j >= n_ready) {  // block-uniform: this token may need a late owner
+            if (threadIdx.x == 0) {
+                uint32_t miss = need[i] & ~ready;
+                for (int o = 0; miss; o++, miss >>= 1)
+                    if ((miss & 1u) && ep_wait_flag(&ret_flags[o], target, err, EP_ERR_WAIT_RET)) ready |= 1u << o;
+            }
+            __syncthreads();
+        }
+        const int t = t0 + i;
+        for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+            const int c = v << 3;
+            float acc[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) acc[q] = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const float w = __half2float(weights[(size_t)t * K + k]);
+                const int r = dest[(size_t)t * K + k];
+                const uint4 qv = __ldcg(reinterpret_cast<const uint4*>(ret + (size_t)r * H + c));  // stored by peers
+                const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float2 f = __half22float2(q2[q]);
+                    acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
+                    acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
+                }
+            }
+            uint4 o;
+            o.x = moe::pack_half2(acc[0], acc[1]);
+            o.y = moe::pack_half2(acc[2], acc[3]);
+            o.z = moe::pack_half2(acc[4], acc[5]);
+            o.w = moe::pack_half2(acc[6], acc[7]);
+            *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
+        }
+    }
 }
 
 }  // namespace
@@ -693,9 +778,9 @@ int p2p_setup(MoeEpContext* c, int64_t T, int64_t H, int64_t E, int64_t K, int64
     }
     size_t o = 0;
     c->off_cnt = o;
-    o += align_up(sizeof(int32_t) * n * E);
+    o += align_up(sizeof(int32_t) * 2 * n * E);  // double-buffered by call parity
     c->off_flags = o;
-    o += align_up(64);
+    o += align_up(sizeof(unsigned long long) * F_WORDS);
     c->off_rows = o;
     o += align_up((size_t)R * H * 2);
     c->off_ret = o;
@@ -772,7 +857,7 @@ int p2p_setup(MoeEpContext* c, int64_t T, int64_t H, int64_t E, int64_t K, int64
         hp.rows[p] = reinterpret_cast<__half*>(b + c->off_rows);
         hp.ret[p] = reinterpret_cast<__half*>(b + c->off_ret);
         hp.flags[p] = reinterpret_cast<unsigned long long*>(b + c->off_flags);
-        hp.ret_flag[p] = hp.flags[p] + 2;
+        hp.ret_flag[p] = hp.flags[p] + F_RET + c->rank;
     }
     if (cudaMalloc(&c->p2p_dev_peers, sizeof(EpPeers)) != cudaSuccess ||
         cudaMemcpy(c->p2p_dev_peers, &hp, sizeof(hp), cudaMemcpyHostToDevice) != cudaSuccess)
@@ -797,7 +882,8 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
 {
     const int n = c->nranks, me = c->rank, El = (int)(E / n);
     const int TK = (int)(T * K);
-    const unsigned long long target = (++c->epoch) * (unsigned long long)n;
+    const unsigned long long target = ++c->epoch;  // call number: every flag is raised once per call
+    const int par = (int)(target & 1u);              // counts buffer of this call
     const EpPeers* dp = static_cast<const EpPeers*>(c->p2p_dev_peers);
     uint8_t* base = static_cast<uint8_t*>(c->p2p_base);
     const int32_t* cnt_local = reinterpret_cast<const int32_t*>(base + c->off_cnt);
@@ -816,8 +902,8 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     int32_t* seg = at<int32_t>(ws, L.seg);
     unsigned long long* row_ptr = at<unsigned long long>(ws, L.xr);  // R entries fit: H*2 >= 8
     __half* hbuf = at<__half>(ws, L.h);
-    unsigned int* done1 = reinterpret_cast<unsigned int*>(flags + 4);
-    unsigned int* done2 = reinterpret_cast<unsigned int*>(flags + 5);
+    unsigned int* done1 = reinterpret_cast<unsigned int*>(flags + F_DONE1);
+    unsigned int* done2 = reinterpret_cast<unsigned int*>(flags + F_DONE2);
     cudaEvent_t* ev = moe::trace_begin_call();
     moe::trace_mark(ev, 0, s);
     // the error word is cleared by the permutation launch below
@@ -829,20 +915,29 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
                             offsets, perm, dest, err, moe::routing_error_word(), s) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
-    ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n);
-    ep_p2p_plan_kernel<<<1, 256, sizeof(int32_t) * E, s>>>(cnt_local, flags, (int)E, El, me, n, (int)R, target, err,
-                                                           disp_base, expoff, seg, overflow);
+    ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n, par);
+    ep_p2p_plan_kernel<<<1, 256, sizeof(int32_t) * E, s>>>(cnt_local, flags, (int)E, El, me, n, par, (int)R, target,
+                                                           err, disp_base, expoff, seg, overflow);
+    ep_p2p_rowptr_kernel<<<El * n < 1024 ? El * n : 1024, 256, 0, s>>>(seg, El * n, n, (int)H, dp, row_ptr);
+    // two blocks (16 warps, one row each at a time) per SM: enough to keep NVLink busy
     int dgrid = (TK + 7) / 8;
-    if (dgrid > 148 * 8) dgrid = 148 * 8;
+    if (dgrid > 2 * 148) dgrid = 2 * 148;
     if (dgrid < 1) dgrid = 1;
     ep_p2p_dispatch_kernel<<<dgrid, 256, 0, s>>>(static_cast<const __half*>(x), perm, offsets, disp_base, overflow, dp,
-                                                 TK, (int)E, El, (int)K, (int)H, n, done1);
-    ep_p2p_rowptr_kernel<<<El * n < 1024 ? El * n : 1024, 256, 0, s>>>(seg, El * n, n, (int)H, dp, row_ptr);
-    ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 1, target, err, EP_ERR_WAIT_ROWS);
+                                                 TK, (int)E, El, (int)K, (int)H, me, n, done1);
     if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 3, s);
+    // GEMM1 starts as soon as this rank's own dispatch is issued; its producer waits,
+    // per tile, only for the sources whose rows the tile covers (dispatch overlapped
+    // with the first tiles).  MOE_EP_SERIAL=1: one wait for every source first
+    // (no overlap; for comparisons).
+    static const bool serial = getenv("MOE_EP_SERIAL") && getenv("MOE_EP_SERIAL")[0] == '1';
+    if (serial)
+        for (int src = 0; src < n; src++)
+            ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + F_ROWS + src, target, err, EP_ERR_WAIT_ROWS);
+    const moe::SourceWait sw = {flags + F_ROWS, seg, n, EP_ERR_WAIT_ROWS, target};
     cudaError_t e = moe::launch_gemm_swiglu(rows_local, static_cast<const __half*>(ewl), expoff, hbuf, err, (int)R,
-                                            (int)H, El, (int)I, 0, s, kEpRowsHint);
+                                            (int)H, El, (int)I, 0, s, kEpRowsHint, serial ? nullptr : &sw);
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 4, s);
@@ -855,12 +950,12 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     if (e == cudaErrorInvalidValue) return MOE_ERR_UNSUPPORTED;
     if (e != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 5, s);
-    // one bounded wait for every owner's returned rows, then the combine through the
-    // inverse permutation (a timed-out wait leaves stale rows; the error word says so)
-    ep_p2p_wait_kernel<<<1, 32, 0, s>>>(flags + 2, target, err, EP_ERR_WAIT_RET);
-    if (T > 0 && moe::launch_combine_indexed(ret_local, dest, wts, static_cast<__half*>(y), (int)T, (int)H, (int)K,
-                                             s) != cudaSuccess)
-        return MOE_ERR_CUDA;
+    // combine on arrival: tokens whose owners have returned their rows first; a
+    // timed-out wait leaves stale rows, and the error word says so
+    if (T > 0)
+        ep_combine_arrival_kernel<<<(int)((T + EP_COMBINE_CH - 1) / EP_COMBINE_CH), 256, 0, s>>>(
+            ret_local, dest, ids, wts, static_cast<__half*>(y), (int)T, (int)H, (int)K, El, n, flags + F_RET, target,
+            err);
     if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
     moe::trace_mark(ev, 6, s);
     return MOE_OK;

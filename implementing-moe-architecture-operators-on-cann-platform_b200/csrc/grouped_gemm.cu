@@ -84,6 +84,16 @@ struct GemmArgs {
     unsigned int* done_counter;
     unsigned long long* const* peer_flags;
     int npeers;
+    // Expert-parallel GEMM1 only (src_flags != nullptr): the A rows arrive from n
+    // source ranks while the kernel runs.  Before loading a tile's rows the producer
+    // waits (bounded) until every source whose rows the tile covers has raised its
+    // flag: src_flags[s] >= src_target.  src_seg[(e*nsrc + s)*3] = {first row, -,
+    // rows} of the (local expert e, source s) block of A.
+    const unsigned long long* src_flags;
+    const int32_t* src_seg;
+    int nsrc;
+    int src_err_code;
+    unsigned long long src_target;
 };
 
 // Paired-CTA variant (PAIR=1): a 2-CTA cluster runs one 256-row tile with M=256
@@ -235,7 +245,11 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         tma_prefetch_desc(&tmB);
     }
     pdl_trigger();
-    pdl_wait();  // offsets, A rows (and perm) come from the previous launches
+    // offsets, A rows (and perm) come from the previous launches.  Expert-parallel
+    // GEMM1 is the exception: it runs alongside the dispatch kernel before it (whose
+    // rows it gates on the sources' flags), and its offsets and segment table come
+    // from a launch that completed before that kernel started.
+    if (!args.src_flags) pdl_wait();
     if (warp == 2) {  // tile prefix: tiles per expert = ceil(rows/ROWS) * n_tiles
         if (lane == 0) {
             int run = 0;
@@ -280,10 +294,27 @@ ffn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             TileCursor<ROWS> cur;
             uint32_t it = 0;
             bool ok = true;
+            uint32_t src_ready = 0;  // sources whose rows have landed (expert-parallel GEMM1)
             for (int tile = unit; ok && tile < total_tiles; tile += nunits) {
                 int e, mt, nt;
                 cur.decode(tail->tile_prefix, offsets, args.n_tiles, tile, e, mt, nt);
                 const int a_row = offsets[e] + mt * ROWS + (int)crank * GM_BM;
+                if (args.src_flags) {
+                    const int a_end = min(a_row + GM_BM, offsets[e + 1]);
+                    for (int sidx = 0; ok && sidx < args.nsrc; sidx++) {
+                        if ((src_ready >> sidx) & 1u) continue;
+                        const int32_t* g = args.src_seg + 3 * (e * args.nsrc + sidx);
+                        const int d0 = g[0], len = g[2];
+                        if (len <= 0 || d0 >= a_end || d0 + len <= a_row) continue;
+                        if (flag_wait_bounded(args.src_flags + sidx, args.src_target, args.err, args.src_err_code,
+                                              abort_flag))
+                            src_ready |= 1u << sidx;
+                        else
+                            ok = false;
+                    }
+                    if (!ok) break;
+                    fence_proxy_async_global();  // the rows were stored by peers' generic stores
+                }
                 const int b_lo = e * args.b_rows_per_expert + args.b_seg + nt * args.b_nstep;
                 const int b_hi = b_lo + args.b_hi_delta;
                 for (int kb = 0; kb < nk; kb++, it++) {
@@ -734,7 +765,7 @@ static cudaError_t launch_down_any(const CUtensorMap& ta, const CUtensorMap& tb,
 // GEMM1: h[rows, I] = SwiGLU(xp @ [Wg; Wu]^T) per expert.
 cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, const int32_t* offsets,
                                __half* h, int* err, int rows_cap, int H, int E, int I, int max_ctas,
-                               cudaStream_t s, int rows_hint)
+                               cudaStream_t s, int rows_hint, const SourceWait* src)
 {
     CUtensorMap ta, tb;
     if (!make_tmap(&ta, xp, (uint64_t)H, (uint64_t)(rows_cap > 0 ? rows_cap : 1)) ||
@@ -754,6 +785,14 @@ cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights, c
     a.b_nstep = 128;
     a.b_hi_delta = I;
     a.out_ld = I;
+    if (src) {
+        if (src->nsrc < 1 || src->nsrc > 32) return cudaErrorInvalidValue;
+        a.src_flags = src->flags;
+        a.src_seg = src->seg;
+        a.nsrc = src->nsrc;
+        a.src_err_code = src->err_code;
+        a.src_target = src->target;
+    }
     return launch_ffn_any<MODE_SWIGLU>(ta, tb, a, rows_cap, rows_hint, max_ctas, true, s);
 }
 

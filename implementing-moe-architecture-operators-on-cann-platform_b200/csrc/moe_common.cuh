@@ -98,6 +98,41 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// ------------------------------------------------------------------ cross-GPU flags
+// Acquire load of a flag another GPU (or this one) raises with a system-scope
+// atomic after its data stores and a system fence.
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait (one thread) until *flag >= target.  Gives up, recording `code` in
+// *err, after MOE_WAIT_LIMIT_NS, or at once when *stop (optional) is nonzero or
+// already holds `code` (another waiter of this launch gave up: one timeout, not
+// one per waiter).
+__device__ __forceinline__ bool flag_wait_bounded(const unsigned long long* flag, unsigned long long target,
+                                                  int* err, int code, volatile int* stop)
+{
+    if (ld_acquire_sys(flag) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        if (ld_acquire_sys(flag) >= target) return true;
+        if ((stop && *stop) || (*reinterpret_cast<volatile int*>(err) & code)) return false;
+        if (global_timer_ns() - t0 > MOE_WAIT_LIMIT_NS) {
+            atomicOr(err, code);
+            if (stop) *stop = 1;
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+// Orders this thread's earlier generic-proxy observations (a flag acquired) before
+// its later async-proxy (TMA) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // ------------------------------------------------------------------ dependent launch
 // Programmatic dependent launch: a kernel lets the next kernel of the stream start
 // its prologue early (pdl_trigger), and that kernel waits for this one's results

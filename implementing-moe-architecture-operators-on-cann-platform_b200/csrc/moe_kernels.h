@@ -49,9 +49,20 @@ cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32
 // extent); rows_hint, when >= 0, is the expected number of rows actually present
 // (used only to choose the tile shape: single-CTA or paired-CTA tiles, and for the
 // down projection wide or narrow ones); allow_pair = false keeps single-CTA tiles.
+// Expert-parallel GEMM1: A rows that arrive from `nsrc` source ranks while the
+// kernel runs (see GemmArgs::src_flags).  seg: [E][nsrc][3] {first row, -, rows}.
+struct SourceWait {
+    const unsigned long long* flags;  // [nsrc], raised by each source when its rows have landed
+    const int32_t* seg;
+    int nsrc;
+    int err_code;                     // recorded in *err when a wait gives up
+    unsigned long long target;
+};
+
 cudaError_t launch_gemm_swiglu(const __half* xp, const __half* expert_weights,
                                const int32_t* offsets, __half* h, int* err, int rows_cap, int H,
-                               int E, int I, int max_ctas, cudaStream_t s, int rows_hint = -1);
+                               int E, int I, int max_ctas, cudaStream_t s, int rows_hint = -1,
+                               const SourceWait* src = nullptr);
 
 cudaError_t launch_gemm_down(const __half* h, const __half* expert_weights, const int32_t* offsets,
                              const int32_t* perm, __half* expert_out, int* err, int rows_cap,
