@@ -124,7 +124,7 @@ constexpr int kChunk = 1024;  // permutation chunk (permute.cu)
 
 struct EpLayout {
     size_t err, chunk_counts, chunk_base, offsets, perm, dest, ids, weights, sendcnt, recvcnt,
-        expoff, seg, row_src, xp, recv, xr, h, total;
+        expoff, seg, row_src, xp, recv, xr, h, tile_counts, tile_rank, total;
 };
 
 // Row hint passed to the grouped GEMM launchers: 0 keeps the expert-parallel GEMMs
@@ -162,6 +162,8 @@ EpLayout ep_layout(int n, int64_t T, int64_t H, int64_t E, int64_t K, int64_t I,
     L.recv = take(2 * (size_t)Rr * H);  // received rows; later GEMM2's output (eo)
     L.xr = take(2 * (size_t)Rr * H);    // received rows, expert-major
     L.h = take(2 * (size_t)Rr * I);
+    L.tile_counts = take(4 * (size_t)(moe::routing_tiles((int)T) > 0 ? moe::routing_tiles((int)T) : 1) * E);
+    L.tile_rank = take(4 * (size_t)TK);
     L.total = o;
     return L;
 }
@@ -644,15 +646,16 @@ int MoeEpLayerForward(MoeEpContext* c, const void* x, const void* w_gate,
     moe::trace_mark(ev, 0, s);
     // 1-2. routing, permutation (with its inverse), gather
     // the error word is cleared by the permutation launch below
+    int32_t* tcounts = at<int32_t>(ws, L.tile_counts);
+    int32_t* trank = at<int32_t>(ws, L.tile_rank);
     if (T > 0) {
         if ((e = moe::launch_routing(static_cast<const __half*>(x), static_cast<const __half*>(w_gate), ids,
-                                     wts, (int)T, (int)H, (int)E, (int)K, s)) != cudaSuccess)
+                                     wts, (int)T, (int)H, (int)E, (int)K, s, tcounts, trank)) != cudaSuccess)
             return MOE_ERR_CUDA;
     }
     moe::trace_mark(ev, 1, s);
-    if ((e = moe::launch_permute(ids, TK, (int)E, at<int32_t>(ws, L.chunk_counts),
-                                 at<int32_t>(ws, L.chunk_base), offsets, perm, dest, err, moe::routing_error_word(),
-                                 s)) != cudaSuccess)
+    if ((e = moe::launch_permute_tiles(ids, tcounts, trank, (int)T, (int)K, (int)E, offsets, perm, dest, err,
+                                       moe::routing_error_word(), s)) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
     if (T > 0 && (e = moe::launch_gather_rows(static_cast<const __half*>(x), perm, offsets, (int)E, (int)K,
@@ -907,12 +910,14 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
     cudaEvent_t* ev = moe::trace_begin_call();
     moe::trace_mark(ev, 0, s);
     // the error word is cleared by the permutation launch below
+    int32_t* tcounts = at<int32_t>(ws, L.tile_counts);
+    int32_t* trank = at<int32_t>(ws, L.tile_rank);
     if (T > 0 && moe::launch_routing(static_cast<const __half*>(x), static_cast<const __half*>(w_gate), ids, wts,
-                                     (int)T, (int)H, (int)E, (int)K, s) != cudaSuccess)
+                                     (int)T, (int)H, (int)E, (int)K, s, tcounts, trank) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 1, s);
-    if (moe::launch_permute(ids, TK, (int)E, at<int32_t>(ws, L.chunk_counts), at<int32_t>(ws, L.chunk_base),
-                            offsets, perm, dest, err, moe::routing_error_word(), s) != cudaSuccess)
+    if (moe::launch_permute_tiles(ids, tcounts, trank, (int)T, (int)K, (int)E, offsets, perm, dest, err,
+                                  moe::routing_error_word(), s) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
     ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n, par);

@@ -29,8 +29,19 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 enum GemmMode { MODE_SWIGLU = 0, MODE_DOWN = 1, MODE_DOWN_PTR = 2 };
 
+// tile_counts [ceil(T/128)][E] / tile_rank [T*K] (both or neither): the routing
+// kernel also writes each 128-token tile's expert histogram and each entry's stable
+// rank inside its tile, for launch_permute_tiles.
 cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights,
-                           int T, int H, int E, int K, cudaStream_t s);
+                           int T, int H, int E, int K, cudaStream_t s, int32_t* tile_counts = nullptr,
+                           int32_t* tile_rank = nullptr);
+
+// The permutation from the routing kernel's tile histograms and ranks (layer calls;
+// the ids are the routing kernel's own, so no id is out of range).
+cudaError_t launch_permute_tiles(const int32_t* ids, const int32_t* tile_counts, const int32_t* tile_rank, int T,
+                                 int K, int E, int32_t* offsets, int32_t* perm, int32_t* dest, int* err, int* fold,
+                                 cudaStream_t s);
+inline int routing_tiles(int T) { return (T + 127) / 128; }
 
 cudaError_t launch_permute(const int32_t* ids, int n, int E, int32_t* chunk_counts,
                            int32_t* chunk_base, int32_t* offsets, int32_t* perm, int32_t* dest,

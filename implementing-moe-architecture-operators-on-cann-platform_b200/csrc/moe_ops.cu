@@ -105,7 +105,7 @@ FfnLayout ffn_layout(int64_t T, int64_t H, int64_t E, int64_t K, int64_t I)
 
 struct LayerLayout {
     FfnLayout f;
-    size_t ids, weights, expert_out, total;
+    size_t ids, weights, expert_out, tile_counts, tile_rank, total;
 };
 
 LayerLayout layer_layout(int64_t T, int64_t H, int64_t E, int64_t K, int64_t I)
@@ -120,6 +120,10 @@ LayerLayout layer_layout(int64_t T, int64_t H, int64_t E, int64_t K, int64_t I)
     o += align_up(n * 2);
     L.expert_out = o;
     o += align_up(n * (size_t)H * 2);
+    L.tile_counts = o;  // routing's per-tile expert histograms and in-tile ranks
+    o += align_up(sizeof(int32_t) * (size_t)(moe::routing_tiles((int)T) > 0 ? moe::routing_tiles((int)T) : 1) * E);
+    L.tile_rank = o;
+    o += align_up(n * 4);
     L.total = o;
     return L;
 }
@@ -155,13 +159,17 @@ int run_permute(const int32_t* ids, int64_t T, int64_t K, int64_t E, void* ws, c
     return cuda_status(e);
 }
 
+// tiles: the routing kernel's tile histograms / ranks {tile_counts, tile_rank} when
+// it ran just before (layer calls): the permutation then takes one plain launch.
 int run_ffn(const void* x, const int32_t* ids, const void* ew, void* out, int64_t T, int64_t H,
             int64_t E, int64_t K, int64_t I, void* ws, const FfnLayout& L, cudaStream_t s,
-            cudaEvent_t* ev, int* fold = nullptr)
+            cudaEvent_t* ev, int* fold = nullptr, int32_t* const* tiles = nullptr)
 {
     int32_t* perm = at<int32_t>(ws, L.p.perm);
     int32_t* offsets = at<int32_t>(ws, L.p.offsets);
-    int rc = run_permute(ids, T, K, E, ws, L.p, perm, offsets, s, fold);
+    int rc = tiles ? cuda_status(moe::launch_permute_tiles(ids, tiles[0], tiles[1], (int)T, (int)K, (int)E, offsets,
+                                                           perm, nullptr, at<int>(ws, L.p.err), fold, s))
+                   : run_permute(ids, T, K, E, ws, L.p, perm, offsets, s, fold);
     if (rc != MOE_OK) return rc;
     trace_mark(ev, 2, s);
     if (T == 0) return MOE_OK;
@@ -274,15 +282,17 @@ int MoeLayerForward(const void* x, const void* w_gate, const void* expert_weight
                                L.f, s, nullptr);
     cudaEvent_t* ev = trace_begin_call();
     trace_mark(ev, 0, s);
+    int32_t* tiles[2] = {at<int32_t>(workspace, L.tile_counts), at<int32_t>(workspace, L.tile_rank)};
     int rc = cuda_status(moe::launch_routing(static_cast<const __half*>(x),
                                              static_cast<const __half*>(w_gate), expert_ids,
                                              static_cast<__half*>(weights), (int)T, (int)H, (int)E,
-                                             (int)K, s));
+                                             (int)K, s, tiles[0], tiles[1]));
     if (rc != MOE_OK) return rc;
     trace_mark(ev, 1, s);
-    // the permutation moves a routing wait timeout into this call's error word
+    // the permutation (from the routing kernel's tile histograms) moves a routing
+    // wait timeout into this call's error word
     rc = run_ffn(x, expert_ids, expert_weights, expert_out, T, H, E, K, I, workspace, L.f, s, ev,
-                 moe::routing_error_word());
+                 moe::routing_error_word(), tiles);
     if (rc != MOE_OK) return rc;
     rc = cuda_status(moe::launch_combine(static_cast<const __half*>(expert_out),
                                          static_cast<const __half*>(weights),

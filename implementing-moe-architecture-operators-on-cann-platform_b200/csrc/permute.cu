@@ -240,6 +240,82 @@ __global__ void err_init_kernel(int* err, int* fold)
     *err = fold ? atomicExch(fold, 0) : 0;
 }
 
+// The permutation of a layer call, after the routing kernel has written each
+// 128-token tile's expert histogram (tile_counts [tiles][E]) and each entry's
+// stable rank inside its tile (tile_rank [T*K]): block b derives, for tile b, every
+// expert's first position (all tiles' totals before that expert, plus the entries of
+// the expert in tiles before b) and scatters its entries.  Same order as the
+// counting sort (experts ascending, flat index t*K+k ascending), one ordinary
+// launch, no grid-wide synchronisation.  Block 0 writes offsets and the call's
+// error word (cleared, or the routing error `fold` held).
+constexpr int RT_TILE_TOKENS = 128;  // the routing kernel's tile (routing.cu RT_BM)
+
+__global__ void __launch_bounds__(256)
+perm_tiles_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ tile_counts,
+                  const int32_t* __restrict__ tile_rank, int T, int K, int E, int32_t* __restrict__ offsets,
+                  int32_t* __restrict__ perm, int32_t* __restrict__ dest, int* __restrict__ err, int* fold)
+{
+    extern __shared__ int pt_smem[];
+    int* first = pt_smem;  // [E] first position of expert e's entries of this tile
+    int* tot = pt_smem + E;  // [E] entries of expert e over all tiles
+    pdl_trigger();
+    pdl_wait();  // ids, tile_counts, tile_rank come from the routing launch
+    const int ntiles = gridDim.x, b = blockIdx.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int all = 0, before = 0;
+        for (int c = 0; c < ntiles; c++) {
+            const int v = tile_counts[(size_t)c * E + e];
+            all += v;
+            if (c < b) before += v;
+        }
+        tot[e] = all;
+        first[e] = before;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive scan of the totals (E <= 256)
+        int run = 0;
+        for (int e = 0; e < E; e++) {
+            const int v = tot[e];
+            tot[e] = run;
+            run += v;
+        }
+        if (b == 0) {
+            offsets[E] = run;
+            *err = fold ? atomicExch(fold, 0) : 0;
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        first[e] += tot[e];
+        if (b == 0) offsets[e] = tot[e];
+    }
+    __syncthreads();
+    const long long f0 = (long long)b * RT_TILE_TOKENS * K;
+    const long long f1 = min((long long)T * K, f0 + (long long)RT_TILE_TOKENS * K);
+    for (long long f = f0 + threadIdx.x; f < f1; f += blockDim.x) {
+        const int pos = first[ids[f]] + tile_rank[f];
+        perm[pos] = (int32_t)f;
+        if (dest) dest[f] = pos;
+    }
+}
+
+cudaError_t launch_permute_tiles(const int32_t* ids, const int32_t* tile_counts, const int32_t* tile_rank, int T,
+                                 int K, int E, int32_t* offsets, int32_t* perm, int32_t* dest, int* err, int* fold,
+                                 cudaStream_t s)
+{
+    const int ntiles = (T + RT_TILE_TOKENS - 1) / RT_TILE_TOKENS;
+    if (ntiles == 0) {  // empty batch: offsets all zero, error word initialised
+        cudaError_t e = cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), s);
+        if (e != cudaSuccess) return e;
+        err_init_kernel<<<1, 1, 0, s>>>(err, fold);
+        return cudaGetLastError();
+    }
+    cudaError_t e = launch_pdl(perm_tiles_kernel, dim3(ntiles), dim3(256), (size_t)2 * E * sizeof(int), s, ids,
+                               tile_counts, tile_rank, T, K, E, offsets, perm, dest, err, fold);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 cudaError_t launch_copy_rows(const __half* src, const int32_t* idx, int rows, int H, __half* dst,
                              cudaStream_t s)
 {

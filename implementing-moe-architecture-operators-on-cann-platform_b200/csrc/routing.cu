@@ -86,7 +86,8 @@ template <bool RESIDENT>
 __global__ void __launch_bounds__(RT_THREADS)
 routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restrict__ w_gate,
                   int32_t* __restrict__ expert_ids, __half* __restrict__ weights, int T, int H, int E, int K,
-                  int epad, uint32_t tmem_cols, int nst, int nkl_max, int* err)
+                  int epad, uint32_t tmem_cols, int nst, int nkl_max, int* err, int32_t* __restrict__ tile_counts,
+                  int32_t* __restrict__ tile_rank)
 {
     // A cluster of S CTAs shares one 128-token tile; CTA rank c handles k-blocks
     // [c*nk/S, (c+1)*nk/S) and rank 0 sums the partial logits in rank order.
@@ -110,6 +111,7 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
     int* errp = err ? err : &g_routing_err;
 
     RT_STAMP(0)
+    pdl_trigger();  // the permutation launch after it may be scheduled now (it waits for this grid)
     if (tid == 0) {
         for (int s = 0; s < nst; s++) {
             mbar_init(smem_u32(&tail->full[s]), 1);
@@ -381,18 +383,17 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
     // computes them; ordering by e instead of e / sum can differ only where the
     // division rounds two different exps to one probability (a near tie).
     const int t = t0 + r;
+    int ti[8];  // this token's top-K ids (slot order)
+#pragma unroll
+    for (int j = 0; j < 8; j++) ti[j] = 0;
     if (t < T) {
         const float* l = lg + (size_t)r * pitch;
         float maxv = -1e30f;
         for (int i = 0; i < E; i++) maxv = l[i] > maxv ? l[i] : maxv;
         float sum = 0.0f;
         float tv[8];
-        int ti[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            tv[j] = -1.0f;
-            ti[j] = 0;
-        }
+        for (int j = 0; j < 8; j++) tv[j] = -1.0f;
         for (int i = 0; i < E; i++) {
             float cv = expf(l[i] - maxv);
             sum += cv;
@@ -422,6 +423,48 @@ routing_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __half* __restr
                 expert_ids[(size_t)t * K + j] = ti[j];
                 weights[(size_t)t * K + j] = __float2half_rn(tv[j] / wsum);
             }
+    }
+    if (tile_counts) {
+        // First pass of the permutation, fused (layer calls): this tile's per-expert
+        // histogram, tile_counts[tile][E], and each entry's stable rank among the
+        // tile's entries of its expert, tile_rank[t*K+k], in flat order t*K+k (the
+        // order of tests/moe_cpu_sim.cpp:412-419).  The 128*K entries go in K rounds
+        // of 128 consecutive flat indices; inside a round, a warp match gives the
+        // rank among the warp's lanes and per-warp counts give the rest.
+        __syncthreads();  // every thread is done with the logits: reuse their space
+        int* ids_s = reinterpret_cast<int*>(smem);  // [128*K]
+        int* wcnt = ids_s + RT_BM * K;              // [4 warps][E]
+        int* base = wcnt + 4 * E;                   // [E] entries of each expert so far
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < K) ids_s[r * K + j] = t < T ? ti[j] : -1;
+        for (int i = tid; i < 4 * E; i += RT_THREADS) wcnt[i] = 0;
+        for (int i = tid; i < E; i += RT_THREADS) base[i] = 0;
+        __syncthreads();
+        const int lane = tid & 31;
+        for (int q = 0; q < K; q++) {
+            const int f = q * RT_BM + tid;  // flat index inside the tile
+            const int e = ids_s[f];
+            const unsigned same = __match_any_sync(0xffffffffu, e);
+            const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+            if (e >= 0 && rank_in_warp == 0) wcnt[warp * E + e] = __popc(same);
+            __syncthreads();
+            for (int ee = tid; ee < E; ee += RT_THREADS) {
+                int run = base[ee];
+                for (int w = 0; w < 4; w++) {
+                    const int c = wcnt[w * E + ee];
+                    wcnt[w * E + ee] = run;
+                    run += c;
+                }
+                base[ee] = run;
+            }
+            __syncthreads();
+            if (e >= 0) tile_rank[(size_t)t0 * K + f] = wcnt[warp * E + e] + rank_in_warp;
+            __syncthreads();
+            for (int i = tid; i < 4 * E; i += RT_THREADS) wcnt[i] = 0;
+            __syncthreads();
+        }
+        for (int i = tid; i < E; i += RT_THREADS) tile_counts[(size_t)(t0 / RT_BM) * E + i] = base[i];
     }
     __syncthreads();
     RT_STAMP(5)
@@ -455,7 +498,7 @@ int* routing_error_word()
 }
 
 cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, __half* weights, int T, int H,
-                           int E, int K, cudaStream_t s)
+                           int E, int K, cudaStream_t s, int32_t* tile_counts, int32_t* tile_rank)
 {
     if (T == 0) return cudaSuccess;
     static RtEncodeTiledFn enc = nullptr;
@@ -527,9 +570,9 @@ cudaError_t launch_routing(const __half* x, const __half* w_gate, int32_t* ids, 
     lc.numAttrs = 1;
     int* no_err = nullptr;
     cudaError_t e = resident ? cudaLaunchKernelEx(&lc, routing_tc_kernel<true>, tm, w_gate, ids, weights, T, H, E, K,
-                                                  epad, cols, nst, nkl_max, no_err)
+                                                  epad, cols, nst, nkl_max, no_err, tile_counts, tile_rank)
                              : cudaLaunchKernelEx(&lc, routing_tc_kernel<false>, tm, w_gate, ids, weights, T, H, E, K,
-                                                  epad, cols, nst, nkl_max, no_err);
+                                                  epad, cols, nst, nkl_max, no_err, tile_counts, tile_rank);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
