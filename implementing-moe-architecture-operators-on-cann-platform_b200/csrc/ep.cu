@@ -376,11 +376,39 @@ __global__ void ep_p2p_wait_kernel(const unsigned long long* flag, unsigned long
 
 // Combine on arrival.  Block b owns tokens [b*CH, b*CH+CH).  Slot (t,k) comes back
 // from owner ids[t,k]/El, whose rows are all in once ret_flags[owner] >= target.
-// The block first combines the tokens whose owners have all signalled, then waits
-// (bounded) for the missing owners of the rest, so tokens that do not need a slow
-// owner are not held up by it.  Each token is the same fp32 sum in slot order as
+// Two phases, each spread over all the block's threads: first the tokens whose
+// owners have all signalled, then -- after one thread has waited (bounded) for the
+// missing owners -- the rest; so tokens that do not need a slow owner are not held
+// up by it.  Each token is the same fp32 sum in slot order as
 // combine_indexed_kernel (tests/moe_cpu_sim.cpp:298-305), so y is bit-identical.
-constexpr int EP_COMBINE_CH = 16;
+constexpr int EP_COMBINE_CH = 8;
+
+__device__ __forceinline__ void ep_combine_vec(const __half* __restrict__ ret, const int32_t* __restrict__ dest,
+                                               const __half* __restrict__ weights, __half* __restrict__ y, int t,
+                                               int c, int H, int K)
+{
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc[q] = 0.0f;
+    for (int k = 0; k < K; k++) {
+        const float w = __half2float(weights[(size_t)t * K + k]);
+        const int r = dest[(size_t)t * K + k];
+        const uint4 qv = __ldcg(reinterpret_cast<const uint4*>(ret + (size_t)r * H + c));  // stored by peers
+        const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float2 f = __half22float2(q2[q]);
+            acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
+            acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
+        }
+    }
+    uint4 o;
+    o.x = moe::pack_half2(acc[0], acc[1]);
+    o.y = moe::pack_half2(acc[2], acc[3]);
+    o.z = moe::pack_half2(acc[4], acc[5]);
+    o.w = moe::pack_half2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
+}
 
 __global__ void __launch_bounds__(256)
 ep_combine_arrival_kernel(const __half* __restrict__ ret, const int32_t* __restrict__ dest,
@@ -391,7 +419,6 @@ ep_combine_arrival_kernel(const __half* __restrict__ ret, const int32_t* __restr
     __shared__ uint32_t need[EP_COMBINE_CH];
     __shared__ int order[EP_COMBINE_CH];
     __shared__ int n_ready;
-    __shared__ uint32_t ready;
     const int t0 = blockIdx.x * EP_COMBINE_CH;
     const int cnt = min(EP_COMBINE_CH, T - t0);
     if (threadIdx.x < cnt) {
@@ -403,10 +430,11 @@ ep_combine_arrival_kernel(const __half* __restrict__ ret, const int32_t* __restr
         need[threadIdx.x] = m;
     }
     __syncthreads();
+    uint32_t late = 0;  // thread 0: owners not yet in at the first look
     if (threadIdx.x == 0) {
         uint32_t all = 0, rd = 0;
         for (int i = 0; i < cnt; i++) all |= need[i];
-        for (int o = 0; o < 32; o++)  // one look at each owner this block needs
+        for (int o = 0; o < n; o++)  // one look at each owner this block needs
             if (((all >> o) & 1u) && moe::ld_acquire_sys(&ret_flags[o]) >= target) rd |= 1u << o;
         int j = 0;
         for (int i = 0; i < cnt; i++)
@@ -414,45 +442,23 @@ ep_combine_arrival_kernel(const __half* __restrict__ ret, const int32_t* __restr
         n_ready = j;
         for (int i = 0; i < cnt; i++)
             if (need[i] & ~rd) order[j++] = i;
-        ready = rd;
+        late = all & ~rd;
     }
     __syncthreads();
     const int vpr = H >> 3;
-    for (int j = 0; j < cnt; j++) {
-        const int i = order[j];
-        if (j >= n_ready) {  // block-uniform: this token may need a late owner
-            if (threadIdx.x == 0) {
-                uint32_t miss = need[i] & ~ready;
-                for (int o = 0; miss; o++, miss >>= 1)
-                    if ((miss & 1u) && ep_wait_flag(&ret_flags[o], target, err, EP_ERR_WAIT_RET)) ready |= 1u << o;
-            }
-            __syncthreads();
-        }
-        const int t = t0 + i;
-        for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
-            const int c = v << 3;
-            float acc[8];
-#pragma unroll
-            for (int q = 0; q < 8; q++) acc[q] = 0.0f;
-            for (int k = 0; k < K; k++) {
-                const float w = __half2float(weights[(size_t)t * K + k]);
-                const int r = dest[(size_t)t * K + k];
-                const uint4 qv = __ldcg(reinterpret_cast<const uint4*>(ret + (size_t)r * H + c));  // stored by peers
-                const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const float2 f = __half22float2(q2[q]);
-                    acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
-                    acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
-                }
-            }
-            uint4 o;
-            o.x = moe::pack_half2(acc[0], acc[1]);
-            o.y = moe::pack_half2(acc[2], acc[3]);
-            o.z = moe::pack_half2(acc[4], acc[5]);
-            o.w = moe::pack_half2(acc[6], acc[7]);
-            *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
-        }
+    const int nr = n_ready;
+    for (int it = threadIdx.x; it < nr * vpr; it += blockDim.x) {  // tokens with every owner in
+        const int j = it / vpr;
+        ep_combine_vec(ret, dest, weights, y, t0 + order[j], (it - j * vpr) << 3, H, K);
+    }
+    if (nr == cnt) return;  // block-uniform
+    if (threadIdx.x == 0)
+        for (int o = 0; late; o++, late >>= 1)
+            if (late & 1u) ep_wait_flag(&ret_flags[o], target, err, EP_ERR_WAIT_RET);
+    __syncthreads();
+    for (int it = nr * vpr + threadIdx.x; it < cnt * vpr; it += blockDim.x) {  // the rest
+        const int j = it / vpr;
+        ep_combine_vec(ret, dest, weights, y, t0 + order[j], (it - j * vpr) << 3, H, K);
     }
 }
 
