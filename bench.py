@@ -569,9 +569,9 @@ def run_ours(args):
                     "per_rank_copy_gbs": [{"h2d": xbytes * e2e_steps / (c[0].item() / 1e3) / 1e9,
                                            "d2h": xbytes * e2e_steps / (c[1].item() / 1e3) / 1e9} for c in copies]},
             # per step, one GPU: routing, fused permute, gather, gate/up GEMM, down GEMM,
-            # combine; expert parallel: routing, permute, counts, plan, dispatch,
-            # row-pointer, gate/up GEMM (waits per source), down GEMM, combine on arrival
-            "gpu_launches": args.steps * (9 if world > 1 else 6),
+            # combine; expert parallel: routing, permute, counts + plan + return addresses,
+            # dispatch, gate/up GEMM (waits per source), down GEMM, combine on arrival
+            "gpu_launches": args.steps * (7 if world > 1 else 6),
             "clocks": clk.summary(),
         }
         if ep_parity is not None:

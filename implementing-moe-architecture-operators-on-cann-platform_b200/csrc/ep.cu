@@ -226,11 +226,23 @@ __device__ bool ep_wait_flag(const unsigned long long* flag, unsigned long long 
     return moe::flag_wait_bounded(flag, target, err, code, nullptr);
 }
 
-// Writes this rank's per-expert counts into row `me` of buffer `par` of every
-// peer's cnt inbox, then raises its counts flag there.
-__global__ void ep_p2p_counts_kernel(const EpPeers* __restrict__ peers, const int32_t* __restrict__ offsets, int E,
-                                     int me, int n, int par)
+// Counts exchange and plan in one block.  First this rank's per-expert counts go to
+// every peer (as ep_p2p_counts_kernel); then, once every source's counts are in:
+// for each global expert e the row in its owner's inbox where this rank's rows
+// start (disp_base[e]); this rank's expert-major offsets (expoff[El+1]); for each
+// (local expert, source) {first inbox row, row index in the source's permuted
+// order, rows} (seg); and the return address of every inbox row (row_ptr: the
+// source's ret inbox, at the row's index in the source's permuted order).
+__global__ void __launch_bounds__(256)
+ep_p2p_plan_kernel(const EpPeers* __restrict__ peers, const int32_t* __restrict__ offsets,
+                   const int32_t* __restrict__ cnt_all, const unsigned long long* flags, int E, int El, int me,
+                   int n, int par, int R, int H, unsigned long long target, int* err,
+                   int32_t* __restrict__ disp_base, int32_t* __restrict__ expoff, int32_t* __restrict__ seg,
+                   int32_t* __restrict__ overflow, unsigned long long* __restrict__ row_ptr)
 {
+    __shared__ int ok;
+    __shared__ int over;
+    extern __shared__ int32_t pl_tot[];  // [E] rows per global expert over all sources
     for (int p = 0; p < n; p++)
         for (int e = threadIdx.x; e < E; e += blockDim.x)
             peers->cnt[p][((size_t)par * n + me) * E + e] = offsets[e + 1] - offsets[e];
@@ -240,20 +252,6 @@ __global__ void ep_p2p_counts_kernel(const EpPeers* __restrict__ peers, const in
         __threadfence_system();
         atomicAdd_system(&peers->flags[threadIdx.x][F_CNT + me], 1ull);
     }
-}
-
-// Plan, on the device, once every source's counts are in: for each global expert e
-// the row in its owner's inbox where this rank's rows start (disp_base[e]); this
-// rank's expert-major offsets (expoff[El+1]) and, for each (local expert, source),
-// {first inbox row, row index in the source's permuted order, rows} (seg).
-__global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt_all, const unsigned long long* flags, int E,
-                                   int El, int me, int n, int par, int R, unsigned long long target, int* err,
-                                   int32_t* __restrict__ disp_base, int32_t* __restrict__ expoff,
-                                   int32_t* __restrict__ seg, int32_t* __restrict__ overflow)
-{
-    __shared__ int ok;
-    __shared__ int over;
-    extern __shared__ int32_t pl_tot[];  // [E] rows per global expert over all sources
     if (threadIdx.x == 0) {
         int good = 1;
         for (int s = 0; s < n && good; s++) good = ep_wait_flag(&flags[F_CNT + s], target, err, EP_ERR_WAIT_COUNTS);
@@ -310,6 +308,14 @@ __global__ void ep_p2p_plan_kernel(const int32_t* __restrict__ cnt_all, const un
         seg[3 * i + 1] = (int32_t)rb;
         seg[3 * i + 2] = cnt[s * E + e];
     }
+    __syncthreads();
+    for (int i = 0; i < El * n; i++) {  // return address of every inbox row
+        const int s = i % n;
+        const int d0 = seg[3 * i], rb = seg[3 * i + 1], len = seg[3 * i + 2];
+        __half* base = peers->ret[s];
+        for (int j = threadIdx.x; j < len; j += blockDim.x)
+            row_ptr[d0 + j] = reinterpret_cast<unsigned long long>(base + (size_t)(rb + j) * H);
+    }
 }
 
 // Fused gather + dispatch: row r of this rank's permuted order (expert e) goes from
@@ -351,20 +357,6 @@ ep_p2p_dispatch_kernel(const __half* __restrict__ x, const int32_t* __restrict__
             __threadfence_system();
             for (int p = 0; p < n; p++) atomicAdd_system(&peers->flags[p][F_ROWS + me], 1ull);
         }
-    }
-}
-
-// Destination of every inbox row after the down GEMM: the source rank's ret inbox,
-// at the row's index in that source's permuted order.
-__global__ void ep_p2p_rowptr_kernel(const int32_t* __restrict__ seg, int nseg, int n, int H,
-                                     const EpPeers* __restrict__ peers, unsigned long long* __restrict__ row_ptr)
-{
-    for (int i = blockIdx.x; i < nseg; i += gridDim.x) {
-        const int s = i % n;
-        const int d0 = seg[3 * i], rb = seg[3 * i + 1], len = seg[3 * i + 2];
-        __half* base = peers->ret[s];
-        for (int j = threadIdx.x; j < len; j += blockDim.x)
-            row_ptr[d0 + j] = reinterpret_cast<unsigned long long>(base + (size_t)(rb + j) * H);
     }
 }
 
@@ -926,10 +918,9 @@ int p2p_forward(MoeEpContext* c, const void* x, const void* w_gate, const void* 
                                   moe::routing_error_word(), s) != cudaSuccess)
         return MOE_ERR_CUDA;
     moe::trace_mark(ev, 2, s);
-    ep_p2p_counts_kernel<<<1, 256, 0, s>>>(dp, offsets, (int)E, me, n, par);
-    ep_p2p_plan_kernel<<<1, 256, sizeof(int32_t) * E, s>>>(cnt_local, flags, (int)E, El, me, n, par, (int)R, target,
-                                                           err, disp_base, expoff, seg, overflow);
-    ep_p2p_rowptr_kernel<<<El * n < 1024 ? El * n : 1024, 256, 0, s>>>(seg, El * n, n, (int)H, dp, row_ptr);
+    ep_p2p_plan_kernel<<<1, 256, sizeof(int32_t) * E, s>>>(dp, offsets, cnt_local, flags, (int)E, El, me, n, par,
+                                                           (int)R, (int)H, target, err, disp_base, expoff, seg,
+                                                           overflow, row_ptr);
     // two blocks (16 warps, one row each at a time) per SM: enough to keep NVLink busy
     int dgrid = (TK + 7) / 8;
     if (dgrid > 2 * 148) dgrid = 2 * 148;
