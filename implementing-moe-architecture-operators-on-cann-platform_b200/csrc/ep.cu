@@ -344,7 +344,18 @@ ep_p2p_dispatch_kernel(const __half* __restrict__ x, const int32_t* __restrict__
             const int p = e / El;
             const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(perm[r] / K) * H);
             uint4* dst = reinterpret_cast<uint4*>(peers->rows[p] + (size_t)(disp_base[e] + r - offsets[e]) * H);
-            for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+            // all of a lane's loads of a chunk first, then its stores: one memory latency
+            // per 4 KB of row instead of one per 16 bytes (the grid is small by design)
+            constexpr int VPL = 8;
+            for (int v0 = lane; v0 < nv; v0 += 32 * VPL) {
+                uint4 buf[VPL];
+#pragma unroll
+                for (int u = 0; u < VPL; u++)
+                    if (v0 + 32 * u < nv) buf[u] = __ldg(src + v0 + 32 * u);
+#pragma unroll
+                for (int u = 0; u < VPL; u++)
+                    if (v0 + 32 * u < nv) dst[v0 + 32 * u] = buf[u];
+            }
         }
     }
     __threadfence_system();
