@@ -226,8 +226,9 @@ __device__ bool ep_wait_flag(const unsigned long long* flag, unsigned long long 
     return moe::flag_wait_bounded(flag, target, err, code, nullptr);
 }
 
-// Counts exchange and plan in one block.  First this rank's per-expert counts go to
-// every peer (as ep_p2p_counts_kernel); then, once every source's counts are in:
+// Counts exchange and plan in one block.  First this rank's per-expert counts go
+// into row `me` of buffer `par` of every peer's cnt inbox, and its counts flag is
+// raised there; then, once every source's counts are in:
 // for each global expert e the row in its owner's inbox where this rank's rows
 // start (disp_base[e]); this rank's expert-major offsets (expoff[El+1]); for each
 // (local expert, source) {first inbox row, row index in the source's permuted
